@@ -1,0 +1,35 @@
+// common.cuh — shared declarations of the libenigma_cuda translation units.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "../../include/enigma_cuda.h"
+#include "sm100.cuh"
+
+namespace enigma {
+
+// SM count of the current device (cached per device).
+int sm_count();
+
+// Device word that bounded waits set on timeout (one per device, zeroed at init).
+uint32_t* device_status();
+
+// Operator launchers (asynchronous).  Arguments are validated by the C ABI layer.
+cudaError_t rmsnorm_launch(int dtype, const void* x, const void* w, void* y, int64_t rows,
+                           int64_t hidden, float eps, cudaStream_t s);
+cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                             int64_t K, cudaStream_t s);
+cudaError_t gemm_f32_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                            int64_t K, bool accumulate, cudaStream_t s);
+cudaError_t sdpa_f32_launch(const void* Q, const void* K, const void* V, void* O, int64_t B,
+                            int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
+                            float scale, bool causal, cudaStream_t s);
+cudaError_t sdpa_bf16_launch(const void* Q, const void* K, const void* V, void* O, int64_t B,
+                             int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
+                             float scale, bool causal, cudaStream_t s);
+
+// Records a message for enigma_last_error on the calling thread.
+void set_error(const char* fmt, ...);
+
+}  // namespace enigma

@@ -1,0 +1,192 @@
+// ops_abi.cu — C-ABI operator entry points, generic dispatch by kernel id and
+// event timing.  Validation happens here; kernels assume valid arguments.
+#include <cstdio>
+
+#include "common.cuh"
+
+using enigma::set_error;
+
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int32_t launch_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return ENIGMA_OK;
+  set_error("%s launch failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+  return ENIGMA_ERR_LAUNCH;
+}
+
+int32_t bad(const char* msg) {
+  set_error("bad argument: %s", msg);
+  return ENIGMA_ERR_BADARG;
+}
+
+bool aligned(const void* p, size_t a) { return reinterpret_cast<uintptr_t>(p) % a == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int32_t enigma_rmsnorm(int32_t dtype, const void* x, const void* w, void* y, int64_t rows,
+                       int64_t hidden, float eps, void* stream) {
+  if (dtype != ENIGMA_DTYPE_F32 && dtype != ENIGMA_DTYPE_BF16) return bad("rmsnorm dtype");
+  if (rows < 0 || hidden <= 0) return bad("rmsnorm needs rows >= 0 and hidden > 0");
+  if (rows > 0 && (x == nullptr || w == nullptr || y == nullptr))
+    return bad("rmsnorm: NULL buffer");
+  const size_t es = dtype == ENIGMA_DTYPE_F32 ? 4 : 2;
+  if (!aligned(x, es) || !aligned(w, es) || !aligned(y, es))
+    return bad("rmsnorm: buffers must be aligned to the element size");
+  if (!(eps >= 0.0f)) return bad("rmsnorm: eps must be >= 0");
+  return launch_status(
+      enigma::rmsnorm_launch(dtype, x, w, y, rows, hidden, eps, as_stream(stream)), "rmsnorm");
+}
+
+int32_t enigma_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                         void* stream) {
+  if (M < 0 || N < 0 || K < 0) return bad("gemm: negative size");
+  if (M > (1ll << 31) - 1 || N > (1ll << 31) - 1 || K > (1ll << 31) - 1)
+    return bad("gemm: sizes must fit in int32");
+  if (M == 0 || N == 0) return ENIGMA_OK;
+  if (A == nullptr || B == nullptr || C == nullptr) return bad("gemm: NULL buffer");
+  if (!aligned(A, 2) || !aligned(B, 2) || !aligned(C, 2)) return bad("gemm: misaligned buffer");
+  return launch_status(enigma::gemm_bf16_launch(A, B, C, M, N, K, as_stream(stream)), "gemm");
+}
+
+int32_t enigma_sdpa_bf16(const void* Q, const void* K, const void* V, void* O, int64_t batch,
+                         int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
+                         int64_t head_dim, float scale, int32_t causal, void* stream) {
+  if (batch < 0 || heads_q <= 0 || heads_kv <= 0 || seq_q < 0 || seq_kv < 0 || head_dim <= 0)
+    return bad("sdpa: sizes must be positive");
+  if (heads_q % heads_kv != 0) return bad("sdpa: heads_q must be a multiple of heads_kv");
+  if (head_dim > 256) return bad("sdpa: head_dim must be <= 256");
+  if (batch == 0 || seq_q == 0) return ENIGMA_OK;
+  if (seq_kv == 0) return bad("sdpa: seq_kv must be > 0 when seq_q > 0");
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) return bad("sdpa: NULL buffer");
+  if (!aligned(Q, 2) || !aligned(K, 2) || !aligned(V, 2) || !aligned(O, 2))
+    return bad("sdpa: misaligned buffer");
+  return launch_status(enigma::sdpa_bf16_launch(Q, K, V, O, batch, heads_q, heads_kv, seq_q,
+                                                seq_kv, head_dim, scale, causal != 0,
+                                                as_stream(stream)),
+                       "sdpa");
+}
+
+int32_t enigma_gemm_f32(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                        int32_t accumulate, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return bad("gemm: negative size");
+  if (M > (1ll << 31) - 1 || N > (1ll << 31) - 1 || K > (1ll << 31) - 1)
+    return bad("gemm: sizes must fit in int32");
+  if (M == 0 || N == 0) return ENIGMA_OK;
+  if (A == nullptr || B == nullptr || C == nullptr) return bad("gemm: NULL buffer");
+  if (!aligned(A, 4) || !aligned(B, 4) || !aligned(C, 4)) return bad("gemm: misaligned buffer");
+  return launch_status(enigma::gemm_f32_launch(A, B, C, M, N, K, accumulate != 0,
+                                               as_stream(stream)),
+                       "gemm_f32");
+}
+
+int32_t enigma_sdpa_f32(const void* Q, const void* K, const void* V, void* O, int64_t batch,
+                        int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
+                        int64_t head_dim, float scale, int32_t causal, void* stream) {
+  if (batch < 0 || heads_q <= 0 || heads_kv <= 0 || seq_q < 0 || seq_kv < 0 || head_dim <= 0)
+    return bad("sdpa: sizes must be positive");
+  if (heads_q % heads_kv != 0) return bad("sdpa: heads_q must be a multiple of heads_kv");
+  if (head_dim > 256) return bad("sdpa: head_dim must be <= 256");
+  if (batch == 0 || seq_q == 0) return ENIGMA_OK;
+  if (seq_kv == 0) return bad("sdpa: seq_kv must be > 0 when seq_q > 0");
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) return bad("sdpa: NULL buffer");
+  if (!aligned(Q, 4) || !aligned(K, 4) || !aligned(V, 4) || !aligned(O, 4))
+    return bad("sdpa: misaligned buffer");
+  return launch_status(enigma::sdpa_f32_launch(Q, K, V, O, batch, heads_q, heads_kv, seq_q, seq_kv,
+                                               head_dim, scale, causal != 0, as_stream(stream)),
+                       "sdpa_f32");
+}
+
+int32_t enigma_dispatch(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
+                        const int64_t* ip, int32_t n_ip, const float* fp, int32_t n_fp,
+                        const uint32_t* grid3, const uint32_t* threads3, void* stream) {
+  (void)grid3;
+  (void)threads3;
+  if (n_buffers > 0 && buffers == nullptr) return bad("dispatch: buffers is NULL");
+  if (n_ip > 0 && ip == nullptr) return bad("dispatch: iparams is NULL");
+  if (n_fp > 0 && fp == nullptr) return bad("dispatch: fparams is NULL");
+  switch (kernel_id) {
+    case ENIGMA_KERNEL_RMSNORM:
+      if (n_buffers != 3 || n_ip != 3 || n_fp != 1)
+        return bad("rmsnorm dispatch wants 3 buffers, 3 int params, 1 float param");
+      return enigma_rmsnorm(static_cast<int32_t>(ip[2]), buffers[0], buffers[1], buffers[2], ip[0],
+                            ip[1], fp[0], stream);
+    case ENIGMA_KERNEL_GEMM:
+      if (n_buffers != 3 || n_ip != 5)
+        return bad("gemm dispatch wants 3 buffers, 5 int params (M, N, K, dtype, accumulate)");
+      if (ip[3] == ENIGMA_DTYPE_F32)
+        return enigma_gemm_f32(buffers[0], buffers[1], buffers[2], ip[0], ip[1], ip[2],
+                               static_cast<int32_t>(ip[4]), stream);
+      if (ip[4] != 0) return bad("gemm dispatch: accumulate is fp32-only");
+      return enigma_gemm_bf16(buffers[0], buffers[1], buffers[2], ip[0], ip[1], ip[2], stream);
+    case ENIGMA_KERNEL_SDPA:
+      if (n_buffers != 4 || n_ip != 8 || n_fp != 1)
+        return bad("sdpa dispatch wants 4 buffers, 8 int params, 1 float param");
+      if (ip[7] == ENIGMA_DTYPE_F32)
+        return enigma_sdpa_f32(buffers[0], buffers[1], buffers[2], buffers[3], ip[0], ip[1], ip[2],
+                               ip[3], ip[4], ip[5], fp[0], static_cast<int32_t>(ip[6]), stream);
+      return enigma_sdpa_bf16(buffers[0], buffers[1], buffers[2], buffers[3], ip[0], ip[1], ip[2],
+                              ip[3], ip[4], ip[5], fp[0], static_cast<int32_t>(ip[6]), stream);
+    default: {
+      char msg[64];
+      snprintf(msg, sizeof(msg), "unknown kernel id %d", kernel_id);
+      return bad(msg);
+    }
+  }
+}
+
+int32_t enigma_dispatch_timed(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
+                              const int64_t* ip, int32_t n_ip, const float* fp, int32_t n_fp,
+                              const uint32_t* grid3, const uint32_t* threads3, void* stream,
+                              double* elapsed_us) {
+  if (elapsed_us == nullptr) return bad("elapsed_us is NULL");
+  cudaEvent_t a, b;
+  if (cudaEventCreate(&a) != cudaSuccess) return launch_status(cudaGetLastError(), "event");
+  if (cudaEventCreate(&b) != cudaSuccess) {
+    cudaEventDestroy(a);
+    return launch_status(cudaGetLastError(), "event");
+  }
+  cudaEventRecord(a, as_stream(stream));
+  int32_t rc = enigma_dispatch(kernel_id, buffers, n_buffers, ip, n_ip, fp, n_fp, grid3, threads3,
+                               stream);
+  cudaEventRecord(b, as_stream(stream));
+  if (rc == ENIGMA_OK) rc = enigma_synchronize(stream);
+  if (rc == ENIGMA_OK) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, a, b);
+    *elapsed_us = double(ms) * 1000.0;
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  return rc;
+}
+
+int32_t enigma_event_create(void** ev) {
+  if (ev == nullptr) return bad("ev is NULL");
+  cudaEvent_t e = nullptr;
+  cudaError_t r = cudaEventCreate(&e);
+  *ev = e;
+  return launch_status(r, "event create");
+}
+int32_t enigma_event_destroy(void* ev) {
+  if (ev == nullptr) return ENIGMA_OK;
+  return launch_status(cudaEventDestroy(static_cast<cudaEvent_t>(ev)), "event destroy");
+}
+int32_t enigma_event_record(void* ev, void* stream) {
+  if (ev == nullptr) return bad("ev is NULL");
+  return launch_status(cudaEventRecord(static_cast<cudaEvent_t>(ev), as_stream(stream)),
+                       "event record");
+}
+int32_t enigma_event_elapsed_ms(void* start, void* stop, float* ms) {
+  if (start == nullptr || stop == nullptr || ms == nullptr) return bad("event elapsed: NULL");
+  cudaError_t e = cudaEventSynchronize(static_cast<cudaEvent_t>(stop));
+  if (e != cudaSuccess) return launch_status(e, "event sync");
+  return launch_status(
+      cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop)),
+      "event elapsed");
+}
+
+}  // extern "C"

@@ -1,0 +1,258 @@
+// runtime.cu — the C ABI declared in include/enigma_cuda.h.
+//
+// It plays the part of the reference's Swift runtime
+// (enigma/runtime_dispatch/swift/libenigma_runtime.swift): device and queue
+// creation, buffers, dispatch by kernel, timed dispatch and capability queries.
+// Argument checks happen here, before anything is launched, and map to
+// ENIGMA_ERR_BADARG with a message for enigma_last_error.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace enigma {
+
+namespace {
+thread_local char g_err[512] = {0};
+std::mutex g_mu;
+constexpr int kMaxDev = 64;
+int g_sms[kMaxDev] = {0};
+uint32_t* g_status[kMaxDev] = {nullptr};
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+// Make sure the per-device state (SM count, status word) exists.
+cudaError_t ensure_device_state(int dev) {
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_status[dev] != nullptr) return cudaSuccess;
+  int sms = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  uint32_t* st = nullptr;
+  e = cudaMalloc(&st, 256);
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(st, 0, 256);
+  if (e != cudaSuccess) return e;
+  g_sms[dev] = sms;
+  g_status[dev] = st;
+  return cudaSuccess;
+}
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int sm_count() {
+  const int d = current_device();
+  if (ensure_device_state(d) != cudaSuccess) return 148;
+  return g_sms[d];
+}
+
+uint32_t* device_status() {
+  const int d = current_device();
+  if (ensure_device_state(d) != cudaSuccess) return nullptr;
+  return g_status[d];
+}
+
+}  // namespace enigma
+
+using enigma::set_error;
+
+namespace {
+
+int32_t cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return ENIGMA_OK;
+  set_error("%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+  // Errors raised at launch time are launch failures; sticky errors are execution errors.
+  switch (e) {
+    case cudaErrorInvalidValue:
+    case cudaErrorInvalidConfiguration:
+    case cudaErrorInvalidDeviceFunction:
+    case cudaErrorLaunchOutOfResources:
+    case cudaErrorNoKernelImageForDevice:
+    case cudaErrorMemoryAllocation:
+      return ENIGMA_ERR_LAUNCH;
+    case cudaErrorNoDevice:
+    case cudaErrorInvalidDevice:
+    case cudaErrorInsufficientDriver:
+      return ENIGMA_ERR_DEVICE;
+    default:
+      return ENIGMA_ERR_EXEC;
+  }
+}
+
+int32_t badarg(const char* msg) {
+  set_error("bad argument: %s", msg);
+  return ENIGMA_ERR_BADARG;
+}
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int32_t check_ptr(const void* p, const char* name, size_t align) {
+  if (p == nullptr) {
+    set_error("bad argument: %s is NULL", name);
+    return ENIGMA_ERR_BADARG;
+  }
+  if (reinterpret_cast<uintptr_t>(p) % align != 0) {
+    set_error("bad argument: %s is not %zu-byte aligned", name, align);
+    return ENIGMA_ERR_BADARG;
+  }
+  return ENIGMA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t enigma_last_error(char* buf, size_t len) {
+  if (buf == nullptr || len == 0) return ENIGMA_ERR_BADARG;
+  std::strncpy(buf, enigma::g_err, len - 1);
+  buf[len - 1] = 0;
+  return ENIGMA_OK;
+}
+
+int32_t enigma_device_count(int32_t* count) {
+  if (count == nullptr) return badarg("count is NULL");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    return cuda_status(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return ENIGMA_OK;
+}
+
+int32_t enigma_init(int32_t device) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    set_error("no CUDA device available (%s)", cudaGetErrorString(e));
+    return ENIGMA_ERR_DEVICE;
+  }
+  if (device < 0 || device >= n) return badarg("device index out of range");
+  cudaDeviceProp p;
+  e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceProperties");
+  if (p.major != 10) {
+    set_error("device %d is sm_%d%d; this library is built for sm_100a (B200) only", device,
+              p.major, p.minor);
+    return ENIGMA_ERR_DEVICE;
+  }
+  e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  return cuda_status(enigma::ensure_device_state(device), "device state");
+}
+
+int32_t enigma_stream_create(void** stream) {
+  if (stream == nullptr) return badarg("stream is NULL");
+  cudaStream_t s = nullptr;
+  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  *stream = s;
+  return cuda_status(e, "cudaStreamCreate");
+}
+
+int32_t enigma_stream_destroy(void* stream) {
+  if (stream == nullptr) return ENIGMA_OK;
+  return cuda_status(cudaStreamDestroy(as_stream(stream)), "cudaStreamDestroy");
+}
+
+int32_t enigma_take_device_status(int32_t* timeouts) {
+  uint32_t* st = enigma::device_status();
+  if (st == nullptr) return cuda_status(cudaErrorNoDevice, "device status");
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpy(&v, st, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "read device status");
+  if (v != 0) cudaMemset(st, 0, sizeof(uint32_t));
+  if (timeouts) *timeouts = static_cast<int32_t>(v);
+  return ENIGMA_OK;
+}
+
+int32_t enigma_synchronize(void* stream) {
+  cudaError_t e = stream ? cudaStreamSynchronize(as_stream(stream)) : cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "synchronize");
+  int32_t to = 0;
+  int32_t rc = enigma_take_device_status(&to);
+  if (rc != ENIGMA_OK) return rc;
+  if (to != 0) {
+    set_error("a device-side wait exceeded its limit and the kernel gave up");
+    return ENIGMA_ERR_TIMEOUT;
+  }
+  return ENIGMA_OK;
+}
+
+int32_t enigma_device_name(int32_t device, char* buf, size_t len) {
+  if (buf == nullptr || len == 0) return badarg("buffer is NULL");
+  cudaDeviceProp p;
+  cudaError_t e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceProperties");
+  std::strncpy(buf, p.name, len - 1);
+  buf[len - 1] = 0;
+  return ENIGMA_OK;
+}
+
+int32_t enigma_device_attrs(int32_t device, int64_t* sm_count, int64_t* max_smem_per_block,
+                            int64_t* max_threads_per_block, int64_t* total_mem_bytes,
+                            int32_t* cc_major, int32_t* cc_minor) {
+  cudaDeviceProp p;
+  cudaError_t e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceProperties");
+  if (sm_count) *sm_count = p.multiProcessorCount;
+  if (max_smem_per_block) *max_smem_per_block = static_cast<int64_t>(p.sharedMemPerBlockOptin);
+  if (max_threads_per_block) *max_threads_per_block = p.maxThreadsPerBlock;
+  if (total_mem_bytes) *total_mem_bytes = static_cast<int64_t>(p.totalGlobalMem);
+  if (cc_major) *cc_major = p.major;
+  if (cc_minor) *cc_minor = p.minor;
+  return ENIGMA_OK;
+}
+
+int32_t enigma_alloc(void** ptr, size_t bytes) {
+  if (ptr == nullptr) return badarg("ptr is NULL");
+  *ptr = nullptr;
+  if (bytes == 0) bytes = 16;
+  return cuda_status(cudaMalloc(ptr, bytes), "cudaMalloc");
+}
+int32_t enigma_free(void* ptr) {
+  if (ptr == nullptr) return ENIGMA_OK;
+  return cuda_status(cudaFree(ptr), "cudaFree");
+}
+int32_t enigma_host_alloc(void** ptr, size_t bytes) {
+  if (ptr == nullptr) return badarg("ptr is NULL");
+  *ptr = nullptr;
+  if (bytes == 0) bytes = 16;
+  return cuda_status(cudaMallocHost(ptr, bytes), "cudaMallocHost");
+}
+int32_t enigma_host_free(void* ptr) {
+  if (ptr == nullptr) return ENIGMA_OK;
+  return cuda_status(cudaFreeHost(ptr), "cudaFreeHost");
+}
+int32_t enigma_upload(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return ENIGMA_OK;
+  if (dst == nullptr || src == nullptr) return badarg("NULL pointer in upload");
+  return cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, as_stream(stream)),
+                     "upload");
+}
+int32_t enigma_download(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return ENIGMA_OK;
+  if (dst == nullptr || src == nullptr) return badarg("NULL pointer in download");
+  return cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, as_stream(stream)),
+                     "download");
+}
+int32_t enigma_memset(void* dst, int32_t value, size_t bytes, void* stream) {
+  if (bytes == 0) return ENIGMA_OK;
+  if (dst == nullptr) return badarg("NULL pointer in memset");
+  return cuda_status(cudaMemsetAsync(dst, value, bytes, as_stream(stream)), "memset");
+}
+
+}  // extern "C"

@@ -1,0 +1,14 @@
+// sdpa.cu — bf16 attention dispatcher.
+#include "common.cuh"
+
+namespace enigma {
+cudaError_t sdpa_simt_bf16_launch(const void* Q, const void* K, const void* V, void* O, int64_t B,
+                                  int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
+                                  float scale, bool causal, cudaStream_t s);
+
+cudaError_t sdpa_bf16_launch(const void* Q, const void* K, const void* V, void* O, int64_t B,
+                             int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
+                             float scale, bool causal, cudaStream_t s) {
+  return sdpa_simt_bf16_launch(Q, K, V, O, B, Hq, Hkv, Sq, Skv, D, scale, causal, s);
+}
+}  // namespace enigma

@@ -1,0 +1,139 @@
+/* enigma_cuda.h — C ABI of libenigma_cuda.so, the B200 (sm_100a) backend of the
+ * Enigma runtime.
+ *
+ * This library takes the place of the Swift/Metal runtime dylib
+ * (enigma/runtime_dispatch/swift/libenigma_runtime.swift in the reference),
+ * which Python binds with ctypes (enigma/runtime_dispatch/runtime.py:259-316).
+ * Plain pointers and sizes only: device pointers are `void*` from
+ * enigma_alloc (or any CUDA allocation), streams are `void*` holding a
+ * cudaStream_t (NULL = the legacy default stream).
+ *
+ * Every function returns an int32 status:
+ *    0  ENIGMA_OK
+ *   -1  ENIGMA_ERR_LAUNCH   launch failed (the Swift runtime's "encoder" error)
+ *   -2  ENIGMA_ERR_EXEC     execution error reported by the GPU
+ *   -3  ENIGMA_ERR_TIMEOUT  a bounded device-side wait gave up
+ *   -4  ENIGMA_ERR_BADARG   shape / pointer / alignment rejected before launch
+ *   -5  ENIGMA_ERR_DEVICE   no usable sm_100 device
+ * The message of the last failure on the calling thread is returned by
+ * enigma_last_error.  -1 and -2 keep the Swift runtime's meaning
+ * (libenigma_runtime.swift:146-175).
+ */
+#ifndef ENIGMA_CUDA_H
+#define ENIGMA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ENIGMA_OK 0
+#define ENIGMA_ERR_LAUNCH (-1)
+#define ENIGMA_ERR_EXEC (-2)
+#define ENIGMA_ERR_TIMEOUT (-3)
+#define ENIGMA_ERR_BADARG (-4)
+#define ENIGMA_ERR_DEVICE (-5)
+
+/* Element types (storage); accumulation is always fp32. */
+#define ENIGMA_DTYPE_F32 0
+#define ENIGMA_DTYPE_BF16 1
+
+/* Kernel ids for enigma_dispatch (the recognizer in enigma/compiler maps a
+ * traced @enigma.kernel to one of these). */
+#define ENIGMA_KERNEL_RMSNORM 1   /* bufs: x, w, y            ip: rows, hidden, dtype   fp: eps */
+#define ENIGMA_KERNEL_GEMM 2      /* bufs: A, B, C            ip: M, N, K, dtype, accumulate */
+#define ENIGMA_KERNEL_SDPA 3      /* bufs: Q, K, V, O         ip: B, Hq, Hkv, Sq, Skv, D, causal, dtype  fp: scale */
+
+/* ---- device / queue: replaces enigma_create_device, enigma_create_queue
+ *      (libenigma_runtime.swift:10, :19) ---- */
+int32_t enigma_init(int32_t device);
+int32_t enigma_device_count(int32_t* count);
+int32_t enigma_stream_create(void** stream);
+int32_t enigma_stream_destroy(void* stream);
+int32_t enigma_synchronize(void* stream);
+int32_t enigma_last_error(char* buf, size_t len);
+
+/* ---- capability queries: replace enigma_device_name,
+ *      enigma_device_max_threadgroup_memory,
+ *      enigma_device_max_threads_per_threadgroup, enigma_device_supports_family
+ *      (libenigma_runtime.swift:223-260) ---- */
+int32_t enigma_device_name(int32_t device, char* buf, size_t len);
+int32_t enigma_device_attrs(int32_t device, int64_t* sm_count, int64_t* max_smem_per_block,
+                            int64_t* max_threads_per_block, int64_t* total_mem_bytes,
+                            int32_t* cc_major, int32_t* cc_minor);
+
+/* ---- buffers: replace enigma_create_buffer, enigma_create_buffer_empty,
+ *      enigma_buffer_contents, enigma_release (libenigma_runtime.swift:91-124, :216).
+ *      Device memory is not host-visible, so "contents" becomes explicit copies. ---- */
+int32_t enigma_alloc(void** ptr, size_t bytes);
+int32_t enigma_free(void* ptr);
+int32_t enigma_host_alloc(void** ptr, size_t bytes); /* pinned host memory */
+int32_t enigma_host_free(void* ptr);
+int32_t enigma_upload(void* dst_dev, const void* src_host, size_t bytes, void* stream);
+int32_t enigma_download(void* dst_host, const void* src_dev, size_t bytes, void* stream);
+int32_t enigma_memset(void* dst_dev, int32_t value, size_t bytes, void* stream);
+
+/* ---- the hot-path operators (asynchronous on `stream`) ---- */
+
+/* y = x * rsqrt(mean(x^2) + eps) * w per row; x, y [rows, hidden] row-major, w [hidden].
+ * Replaces the dispatch of rmsnorm_kernel (examples/benchmark_rmsnorm.py:31-84)
+ * and of rmsnorm (examples/metal/rmsnorm_handwritten.metal:4-46). */
+int32_t enigma_rmsnorm(int32_t dtype, const void* x, const void* w, void* y, int64_t rows,
+                       int64_t hidden, float eps, void* stream);
+
+/* C[M,N] = A[M,K] * B[K,N], all row-major bf16, fp32 accumulate, bf16 out.
+ * Replaces the dispatch of gemm_async (examples/async_copy_gemm.py:32-79);
+ * semantics of enigma.gemm (enigma/ops/gemm.py:51-167) with beta = 0. */
+int32_t enigma_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                         void* stream);
+
+/* O = softmax(scale * Q K^T [+ causal mask]) V per (batch, head); bf16 in and out,
+ * Q/O [B, Hq, Sq, D], K/V [B, Hkv, Skv, D], GQA maps q-head h to kv-head h / (Hq/Hkv).
+ * causal masks key j > query i + (Skv - Sq) (bottom-right aligned).
+ * Replaces the dispatch of sdpa_enigma (examples/benchmark_sdpa.py:48-158),
+ * fa_naive / fa_tv_kernel (examples/showcase_attention.py:31-125). */
+int32_t enigma_sdpa_bf16(const void* Q, const void* K, const void* V, void* O, int64_t batch,
+                         int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
+                         int64_t head_dim, float scale, int32_t causal, void* stream);
+
+/* fp32 reference-shape variants on CUDA cores (exact fp32 FMA accumulation):
+ * C[M,N] (+)= A[M,K] * B[K,N] — replaces matmul_k4 / gemm_k4
+ * (tests/metal/test_gemm_matmul_runtime.py:20-60); `accumulate` != 0 adds into C. */
+int32_t enigma_gemm_f32(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                        int32_t accumulate, void* stream);
+/* fp32 attention, same layout and masking as enigma_sdpa_bf16 (showcase_attention.py:31-125,
+ * benchmark_sdpa.py:48-150 with the KV de-interleaved). */
+int32_t enigma_sdpa_f32(const void* Q, const void* K, const void* V, void* O, int64_t batch,
+                        int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
+                        int64_t head_dim, float scale, int32_t causal, void* stream);
+
+/* ---- generic dispatch by kernel id: replaces enigma_dispatch /
+ *      enigma_dispatch_timed (libenigma_runtime.swift:132-214).
+ *      grid / threads are Metal-style totals (threads per axis, not groups),
+ *      accepted for interface parity; the kernels pick their own CTA shapes.
+ *      dispatch_timed returns the device time of the launch in microseconds,
+ *      measured with CUDA events on `stream`, and synchronizes. ---- */
+int32_t enigma_dispatch(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
+                        const int64_t* iparams, int32_t n_iparams, const float* fparams,
+                        int32_t n_fparams, const uint32_t* grid3, const uint32_t* threads3,
+                        void* stream);
+int32_t enigma_dispatch_timed(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
+                              const int64_t* iparams, int32_t n_iparams, const float* fparams,
+                              int32_t n_fparams, const uint32_t* grid3, const uint32_t* threads3,
+                              void* stream, double* elapsed_us);
+
+/* ---- event timing (for benchmarks that time a sequence of launches) ---- */
+int32_t enigma_event_create(void** ev);
+int32_t enigma_event_destroy(void* ev);
+int32_t enigma_event_record(void* ev, void* stream);
+int32_t enigma_event_elapsed_ms(void* start, void* stop, float* ms);
+
+/* Number of device-side timeouts flagged since the last call (and reset). */
+int32_t enigma_take_device_status(int32_t* timeouts);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ENIGMA_CUDA_H */

@@ -1,0 +1,125 @@
+"""CPU oracle for the Enigma hot path — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+arm may import this module, and only as the checker or the timed CPU baseline.
+The product path (enigma-dsl_b200/) never calls it.
+
+Each function restates, in numpy, the reference's own numpy check for that
+operator (the reference keeps its checks inline in its examples and tests;
+there are no stored golden arrays).  Parity pins:
+  * rmsnorm          examples/benchmark_rmsnorm.py:117-118 and
+                     examples/qwen_megakernel.py:308-310
+  * sdpa             examples/showcase_attention.py:150-153 (scaled, max-subtracted
+                     softmax) and examples/benchmark_sdpa.py:198-208 (GQA head map
+                     kvh = qh // QMUL).  The reference has no causal variant:
+                     the causal mask here (key j > i + Sk - Sq masked) is
+                     "parity unpinned" beyond the softmax formula.
+  * gemm             tests/metal/test_gemm_matmul_runtime.py:136,166 (`a @ b`),
+                     enigma/ops/gemm.py:144-167 (C += A @ B).
+  * decode layer     examples/qwen_megakernel.py:320-342 (full_decode_np), at the
+                     BASELINE shapes; standard theta RoPE replaces the example's
+                     synthetic angles (unpinned, follows rope_np's half-split
+                     rotation at :313-317).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to the nearest bf16 (ties to even), returned as fp32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    lsb = (u >> 16) & 1
+    r = ((u + 0x7FFF + lsb) >> 16) << 16
+    out = r.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(x), x, out).astype(np.float32)
+
+
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns (uint16), round to nearest even."""
+    return (bf16_round(x).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def from_bf16_bits(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# --------------------------------------------------------------------------- RMSNorm
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """y = x / sqrt(mean(x^2) + eps) * w, per row (benchmark_rmsnorm.py:117-118).
+
+    The mean is accumulated in fp64 so the oracle is more exact than any
+    fp32 device reduction; the result is returned in fp32.
+    """
+    x64 = np.asarray(x, dtype=np.float64)
+    ms = np.mean(x64 * x64, axis=-1, keepdims=True)
+    y = x64 / np.sqrt(ms + eps) * np.asarray(w, dtype=np.float64)
+    return y.astype(np.float32)
+
+
+# --------------------------------------------------------------------------- GEMM
+def gemm(a: np.ndarray, b: np.ndarray, c: np.ndarray | None = None) -> np.ndarray:
+    """C (+)= A @ B in fp32 (test_gemm_matmul_runtime.py:136,166; ops/gemm.py:144-167)."""
+    out = np.asarray(a, dtype=np.float32) @ np.asarray(b, dtype=np.float32)
+    if c is not None:
+        out = out + np.asarray(c, dtype=np.float32)
+    return out.astype(np.float32)
+
+
+# --------------------------------------------------------------------------- SDPA
+def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float, causal: bool = False
+         ) -> np.ndarray:
+    """softmax(scale * Q K^T [+ mask]) V for [B, Hq, Sq, D] / [B, Hkv, Sk, D] inputs.
+
+    Max-subtracted softmax as in showcase_attention.py:150-153; q-head h reads
+    kv-head h // (Hq // Hkv) as in benchmark_sdpa.py:198-208.  fp64 internally.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    bsz, hq, sq, d = q.shape
+    hk, sk = k.shape[1], k.shape[2]
+    g = hq // hk
+    out = np.zeros((bsz, hq, sq, d), dtype=np.float64)
+    mask = None
+    if causal:
+        i = np.arange(sq)[:, None]
+        j = np.arange(sk)[None, :]
+        mask = j > i + (sk - sq)
+    for b in range(bsz):
+        for h in range(hq):
+            s = (q[b, h] @ k[b, h // g].T) * scale
+            if mask is not None:
+                s = np.where(mask, -np.inf, s)
+            m = np.max(s, axis=-1, keepdims=True)
+            m = np.where(np.isfinite(m), m, 0.0)
+            p = np.exp(s - m)
+            den = p.sum(axis=-1, keepdims=True)
+            out[b, h] = np.where(den > 0, (p @ v[b, h // g]) / np.where(den > 0, den, 1.0), 0.0)
+    return out.astype(np.float32)
+
+
+def sdpa_rows(q, k, v, scale, causal, rows):
+    """sdpa restricted to the listed (b, h) pairs: a bounded sample for large shapes."""
+    q = np.asarray(q)
+    hq, hk = q.shape[1], k.shape[1]
+    g = hq // hk
+    res = []
+    for b, h in rows:
+        res.append(sdpa(q[b:b + 1, h:h + 1], k[b:b + 1, h // g:h // g + 1],
+                        v[b:b + 1, h // g:h // g + 1], scale, causal)[0, 0])
+    return np.stack(res)
+
+
+# --------------------------------------------------------------------------- error metrics
+def max_abs(a, b) -> float:
+    return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))))
+
+
+def rel_fro(a, b) -> float:
+    """||a - b||_F / ||b||_F with b the reference."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = np.linalg.norm(b)
+    return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))
