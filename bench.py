@@ -1,0 +1,373 @@
+#!/usr/bin/env python3
+"""Benchmark of the Enigma hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-ops]
+
+Headline (BASELINE metric, config 2 at its largest size): bf16 RMSNorm over
+x [262144, 8192] (fp32 accumulate, eps 1e-6), HBM GB/s, one kernel launch per
+step.  Bytes per step are the algorithmic ones: read x once, write y once,
+read w once (4*rows*hidden + 2*hidden).  Inputs (4 GiB each way) are larger
+than the 126 MB L2, so no flush is needed between steps.
+
+With N > 1 (launched under torchrun, one rank per GPU) each rank processes
+its own full-size row shard (weak scaling, no collective on the data path);
+the timed region is bracketed by a barrier and cuda synchronize, and the
+elapsed time is the max over ranks.
+
+`ops` in the JSON line adds the other hot-path operators at their BASELINE
+headline sizes on rank 0 (GEMM bf16 8192^3, SDPA bf16 [8,32,8192,128]),
+TFLOP/s against the measured bf16 peak.
+
+--impl reference times the reference's own CPU formulation of the same
+operator (the numpy check of examples/benchmark_rmsnorm.py:117-118, restated
+in oracle/numerics.py) on the host cores, on a bounded row sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "enigma-dsl_b200"))
+
+ROWS, HIDDEN, EPS = 262144, 8192, 1e-6
+METRIC = "RMSNorm HBM GB/s (bf16 262144x8192, fp32 accumulate)"
+BYTES_PER_STEP = 4 * ROWS * HIDDEN + 2 * HIDDEN
+# DRAM bytes (read + write) of one rmsnorm launch at this size, from the ncu
+# capture summarised in profiles/rmsnorm_bf16_262144x8192.md (None until captured).
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+def _set_rows(rows: int) -> None:
+    global ROWS, BYTES_PER_STEP, METRIC
+    ROWS = rows
+    BYTES_PER_STEP = 4 * ROWS * HIDDEN + 2 * HIDDEN
+    METRIC = f"RMSNorm HBM GB/s (bf16 {ROWS}x{HIDDEN}, fp32 accumulate)"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                     "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5
+                ).stdout.strip()
+                if out:
+                    self.samples.append([s.strip() for s in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
+        mx = max((float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()),
+                 default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 2 + i and s[2 + i].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- dist plumbing
+def _dist_init(n_gpus: int):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _time_device(fn, steps, stream):
+    """Average device ms of fn() over `steps` launches, CUDA events on `stream`."""
+    import torch
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def _cpu_rmsnorm_sample(sample_rows: int, threads: int):
+    """Time the oracle's numpy RMSNorm on `sample_rows` rows of the workload.
+
+    Returns (seconds, rows).  Rows are split across `threads` Python threads
+    (numpy releases the GIL inside its kernels).
+    """
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import numerics as orc
+    rng = np.random.default_rng(0)
+    x = orc.bf16_round(rng.standard_normal((sample_rows, HIDDEN), dtype=np.float32))
+    w = orc.bf16_round((1 + 0.1 * rng.standard_normal(HIDDEN)).astype(np.float32))
+    chunks = np.array_split(np.arange(sample_rows), threads)
+
+    def work(idx):
+        if len(idx):
+            orc.rmsnorm(x[idx[0]:idx[-1] + 1], w, EPS)
+
+    t0 = time.perf_counter()
+    if threads == 1:
+        work(chunks[0])
+    else:
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(work, chunks))
+    return time.perf_counter() - t0, sample_rows
+
+
+def _cpu_baseline(threads=1, sample_rows=16384):
+    dt, rows = _cpu_rmsnorm_sample(sample_rows, threads)
+    gbs = (4 * rows * HIDDEN + 2 * HIDDEN) / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {ROWS} rows x {HIDDEN} (bf16-rounded inputs, fp64 numpy "
+                      f"oracle, oracle/numerics.py:rmsnorm), {dt:.2f} s"}
+
+
+# ----------------------------------------------------------------------------- our arm
+def _ops_side(hbm_peak, tc_peak, peak_kind):
+    """GEMM / SDPA at their BASELINE headline sizes on this GPU (rank 0 only)."""
+    import torch
+    from enigma import cuda_ops
+    res = {}
+    stream = torch.cuda.current_stream()
+    n = 8192
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = (torch.randn(n, n, device="cuda", generator=g) / math.sqrt(n)).bfloat16()
+    b = torch.randn(n, n, device="cuda", generator=g).bfloat16()
+    c = torch.empty_like(a)
+    for _ in range(3):
+        cuda_ops.gemm(a, b, out=c)
+    ms = _time_device(lambda: cuda_ops.gemm(a, b, out=c), 20, stream)
+    tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
+    res["gemm_bf16_8192"] = {"tflops": round(tf, 1), "ms": round(ms, 4),
+                             "frac": round(tf / tc_peak, 4), "peak": tc_peak,
+                             "peak_kind": peak_kind + " burst"}
+    del a, b, c
+    if os.environ.get("ENIGMA_BENCH_SDPA", "1") == "1" and _sdpa_tc_available():
+        B, H, S, D = 8, 32, 8192, 128
+        q = torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()
+        k = torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()
+        v = torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()
+        o = torch.empty_like(q)
+        for causal in (True, False):
+            fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
+            for _ in range(2):
+                fn()
+            ms = _time_device(fn, 5, stream)
+            fl = (2 if causal else 4) * B * H * S * S * D
+            tf = fl / (ms * 1e-3) / 1e12
+            res[f"sdpa_bf16_{'causal' if causal else 'noncausal'}_8x32x8192x128"] = {
+                "tflops": round(tf, 1), "ms": round(ms, 3), "frac": round(tf / tc_peak, 4),
+                "flops_convention": "causal 2*B*H*S^2*D, non-causal 4*B*H*S^2*D"}
+    return res
+
+
+def _sdpa_tc_available() -> bool:
+    from enigma import _native
+    return hasattr(_native.lib(), "enigma_sdpa_bf16")
+
+
+def run_ours(args):
+    import torch
+    from enigma import _native, cuda_ops
+    rank, world, local = _dist_init(args.gpus)
+    cuda_ops.ensure_device(torch.cuda.current_device())
+    hbm_peak, tc_peak, peak_kind = _peaks()
+    stream = torch.cuda.current_stream()
+
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    x = torch.randn(ROWS, HIDDEN, device="cuda", generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(HIDDEN, device="cuda", generator=g)).bfloat16()
+    y = torch.empty_like(x)
+    step = lambda: cuda_ops.rmsnorm(x, w, EPS, out=y)  # noqa: E731
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = _time_device(step, args.steps, stream)
+        torch.cuda.synchronize()
+    _barrier(world)
+    cuda_ops.synchronize(torch.cuda.current_device())
+    ms_max = _max_over_ranks(ms, world)
+    value = world * BYTES_PER_STEP / (ms_max * 1e-3) / 1e9
+    achieved = BYTES_PER_STEP / (ms * 1e-3) / 1e9  # one launch per step on this rank
+
+    # e2e through the C ABI with host buffers: pinned host x -> device, kernel,
+    # device y -> pinned host, every step, all on one stream.
+    lib = _native.lib()
+    nbytes = ROWS * HIDDEN * 2
+    hx = torch.empty((ROWS, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
+    hy = torch.empty((ROWS, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
+    hx.copy_(x)
+    sp = stream.cuda_stream
+
+    def e2e_step():
+        _native.check(lib.enigma_upload(x.data_ptr(), hx.data_ptr(), nbytes, sp), "upload")
+        _native.check(lib.enigma_rmsnorm(_native.DTYPE_BF16, x.data_ptr(), w.data_ptr(),
+                                         y.data_ptr(), ROWS, HIDDEN, EPS, sp), "rmsnorm")
+        _native.check(lib.enigma_download(hy.data_ptr(), y.data_ptr(), nbytes, sp), "download")
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e2e_ms = _max_over_ranks(_time_device(e2e_step, e2e_steps, stream), world)
+    e2e_value = world * BYTES_PER_STEP / (e2e_ms * 1e-3) / 1e9
+    del hx, hy
+
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (x ~ N(0,1), w ~ 1 + 0.1 N(0,1), torch generator seeded per rank)",
+        "config": {"workload": f"rmsnorm bf16 rows={ROWS} hidden={HIDDEN} eps={EPS} per GPU",
+                   "rows_per_gpu": ROWS, "hidden": HIDDEN, "parallelism": f"row-shard x{world}",
+                   "l2": "inputs (4 GiB) larger than L2; no flush",
+                   "bytes_per_step_per_gpu": BYTES_PER_STEP},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                     "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                     "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
+                     "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                     "algorithmic_bytes_per_launch": BYTES_PER_STEP},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s (algorithmic bytes / e2e time)",
+                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+                "ms_per_step": round(e2e_ms, 3),
+                "path": "C ABI enigma_upload + enigma_rmsnorm + enigma_download, pinned host"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if not args.no_ops:
+        line["ops"] = _ops_side(hbm_peak, tc_peak, peak_kind)
+    if not args.no_cpu:
+        line["cpu_baseline"] = _cpu_baseline(threads=1, sample_rows=args.cpu_rows)
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    sample = args.cpu_rows
+    for _ in range(args.warmup):
+        _cpu_rmsnorm_sample(min(sample, 1024), threads)
+    times = []
+    for _ in range(args.steps):
+        dt, rows = _cpu_rmsnorm_sample(sample, threads)
+        times.append(dt)
+    dt = sum(times) / len(times)
+    gbs = (4 * sample * HIDDEN + 2 * HIDDEN) / dt / 1e9
+    cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+           "sample": f"{sample} of {ROWS} rows x {HIDDEN} per step (numpy restatement of "
+                     "examples/benchmark_rmsnorm.py:117-118 in oracle/numerics.py)"}
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"rmsnorm bf16 rows={ROWS} hidden={HIDDEN} eps={EPS} per GPU",
+                   "note": "reference is Apple-Metal only; its CPU numpy formulation is timed"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-ops", action="store_true", help="skip the GEMM/SDPA side numbers")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--cpu-rows", type=int, default=16384)
+    ap.add_argument("--rows", type=int, default=ROWS,
+                    help="rows per GPU (smaller cases are for profiling only)")
+    args = ap.parse_args()
+    _set_rows(args.rows)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and args.impl == "ours":
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -117,7 +117,9 @@ def test_gemm_f32_k4(cuda, m):
 @pytest.mark.parametrize("b,hq,hk,sq,sk,d,causal", [
     (1, 2, 2, 128, 128, 128, False), (1, 2, 2, 128, 128, 128, True),
     (2, 4, 2, 256, 256, 64, True), (1, 1, 1, 100, 77, 128, False), (1, 1, 1, 77, 100, 128, True),
-    (1, 8, 1, 1, 300, 64, False)])
+    (1, 8, 1, 1, 300, 64, False), (1, 2, 1, 300, 200, 64, True), (1, 2, 2, 2048, 2048, 128, True),
+    (1, 2, 2, 2048, 2048, 128, False), (2, 2, 1, 129, 1000, 64, False), (1, 1, 1, 1, 1, 128, True),
+    (1, 1, 1, 5, 3, 16, False)])
 def test_sdpa_bf16(cuda, b, hq, hk, sq, sk, d, causal):
     import torch
     from enigma import cuda_ops
