@@ -100,6 +100,27 @@ int32_t enigma_sdpa_f32(const void* Q, const void* K, const void* V, void* O, in
                        "sdpa_f32");
 }
 
+int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const void* V, void* O,
+                            int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
+                            int64_t seq_kv, int64_t head_dim, const int64_t* strides12,
+                            float scale, int32_t causal, void* stream) {
+  if (dtype != ENIGMA_DTYPE_F32 && dtype != ENIGMA_DTYPE_BF16) return bad("sdpa: dtype");
+  if (batch < 0 || heads_q <= 0 || heads_kv <= 0 || seq_q < 0 || seq_kv < 0 || head_dim <= 0)
+    return bad("sdpa: sizes must be positive");
+  if (heads_q % heads_kv != 0) return bad("sdpa: heads_q must be a multiple of heads_kv");
+  if (head_dim > 256) return bad("sdpa: head_dim must be <= 256");
+  if (strides12 == nullptr) return bad("sdpa: strides is NULL");
+  for (int i = 0; i < 12; ++i)
+    if (strides12[i] < 0) return bad("sdpa: negative stride");
+  if (batch == 0 || seq_q == 0) return ENIGMA_OK;
+  if (seq_kv == 0) return bad("sdpa: seq_kv must be > 0 when seq_q > 0");
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) return bad("sdpa: NULL buffer");
+  return launch_status(enigma::sdpa_strided_launch(dtype, Q, K, V, O, batch, heads_q, heads_kv,
+                                                   seq_q, seq_kv, head_dim, strides12, scale,
+                                                   causal != 0, as_stream(stream)),
+                       "sdpa_strided");
+}
+
 int32_t enigma_dispatch(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
                         const int64_t* ip, int32_t n_ip, const float* fp, int32_t n_fp,
                         const uint32_t* grid3, const uint32_t* threads3, void* stream) {

@@ -1,0 +1,233 @@
+"""Recognizer: the B200 build's "lowering" step.
+
+The reference lowers a traced kernel to MSL through its MLIR dialect
+(enigma/compiler/compiler.py:133-211).  Here a traced kernel is instead
+identified as one of the hot-path operators the sm_100a library implements
+and bound to that kernel with its parameters.  There is no code generation
+and no fallback: an unrecognised kernel raises EnigmaError.
+
+A Binding holds what the trace fixes (operator, dtype, eps, scale, shapes
+that are compile-time constants, buffer layout variant) and resolves the
+rest at dispatch time from the buffer sizes and launch grid, the way the
+Metal kernels took their extents from the buffers they were bound to.
+
+Fingerprints (op kinds present in the trace, buffer signature):
+  rmsnorm    simd_sum + rsqrt + per-thread vector loads/stores, or the
+             loop form used inside the Qwen layer; 3 buffers (x, w, y)
+             -- examples/benchmark_rmsnorm.py:31-84
+  sdpa_gqa   exp + fmax + simd_sum(dot) with an interleaved KV buffer and a
+             running-max buffer; 4 buffers (Q, KV, M0, O)
+             -- examples/benchmark_sdpa.py:48-158
+  sdpa_rows  exp + fmax + dot inside a carried loop (one query row per
+             thread); 4 buffers (Q, K, V, O)
+             -- examples/showcase_attention.py:31-125
+  gemm       dot of two 4-vectors into C (C = A B, or C += A B when C is
+             also read) -- tests/metal/test_gemm_matmul_runtime.py:20-60;
+             or async 2-D tile copies of A and B into threadgroup memory
+             -- examples/async_copy_gemm.py:32-79 (bound to the GEMM it
+             stages tiles for: the shipped example never multiplies)
+  decode     the Qwen single-layer decode megakernel (26 buffers)
+             -- examples/qwen_megakernel.py:228-269
+"""
+from __future__ import annotations
+
+import math
+from collections import Counter
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+from .._tracing import EnigmaError, IRValue, KernelBuilder
+from ..tensor import Tensor
+from ..tuple import product
+
+
+@dataclass
+class Binding:
+    """Which sm_100a operator a compiled kernel runs, and with what."""
+
+    op: str                                   # rmsnorm | sdpa | gemm | decode
+    dtype: str                                # "float" | "bfloat"
+    params: Dict[str, object] = field(default_factory=dict)
+    layout: str = "dense"                     # buffer layout variant (sdpa: dense|gqa_interleaved)
+
+    def describe(self) -> str:
+        ps = ", ".join(f"{k}={v}" for k, v in sorted(self.params.items()))
+        return f"{self.op}[{self.dtype}, {self.layout}]({ps})"
+
+
+class _Trace:
+    """Queries over a KernelBuilder: op counts, constants, producers."""
+
+    def __init__(self, b: KernelBuilder):
+        self.b = b
+        self.ops = list(b.walk())
+        self.kinds = Counter(op.op for op in self.ops)
+        self.producer = {id(op.result): op for op in self.ops if op.result is not None}
+
+    def has(self, *kinds) -> bool:
+        return all(self.kinds[k] > 0 for k in kinds)
+
+    def const_of(self, v) -> Optional[float]:
+        if not isinstance(v, IRValue):
+            return None
+        op = self.producer.get(id(v))
+        if op is None:
+            return None
+        if op.op == "const":
+            return op.attrs.get("value")
+        if op.op == "cast":
+            return self.const_of(op.operands[0])
+        return None
+
+    def def_of(self, v):
+        return self.producer.get(id(v)) if isinstance(v, IRValue) else None
+
+    def consts(self, dtype_prefix: str = "") -> List:
+        return [op.attrs.get("value") for op in self.ops
+                if op.op == "const" and op.result.dtype.startswith(dtype_prefix)]
+
+    def vec_widths(self) -> List[int]:
+        return [int(op.result.dtype[-1]) for op in self.ops if op.op == "make_vec"]
+
+
+# ----------------------------------------------------------------------------- rmsnorm
+def _rmsnorm_eps(t: _Trace) -> Tuple[Optional[float], Optional[float]]:
+    """eps and the mean divisor from rsqrt(sum / N + eps)."""
+    for op in t.ops:
+        if op.op not in ("rsqrt", "tv_rsqrt"):
+            continue
+        add = t.def_of(op.operands[0])
+        if add is None or add.op not in ("add", "tv_add"):
+            continue
+        a, b = add.operands
+        eps = t.const_of(b)
+        mean = t.def_of(a)
+        if eps is None:
+            eps, mean = t.const_of(a), t.def_of(b)
+        n = None
+        if mean is not None and mean.op in ("div", "tv_div"):
+            n = t.const_of(mean.operands[1])
+        return eps, n
+    return None, None
+
+
+def _match_rmsnorm(t: _Trace, args: tuple) -> Optional[Binding]:
+    if len(t.b.args) != 3 or not t.has("rsqrt", "simd_sum"):
+        return None
+    if t.kinds["exp"] or t.kinds["dot"]:
+        return None
+    eps, n = _rmsnorm_eps(t)
+    if eps is None:
+        return None
+    dtypes = {a[2] for a in t.b.args}
+    if len(dtypes) != 1 or not dtypes <= {"float", "bfloat"}:
+        return None
+    params = {"eps": float(eps)}
+    if n:
+        params["hidden"] = int(n)
+    x = _first_tensor(args, 2)
+    if x is not None:
+        shp = x.layout.shape
+        params["rows"] = product(shp[0])
+        params["hidden"] = product(shp[1])
+    vw = [c for op in t.ops if op.op == "tv_load" for _, c in op.attrs["groups"]]
+    if vw:
+        params["vector_run"] = max(vw)
+    return Binding("rmsnorm", dtypes.pop(), params)
+
+
+def _first_tensor(args, rank: int) -> Optional[Tensor]:
+    for a in args or ():
+        if isinstance(a, Tensor) and a.layout is not None:
+            s = a.layout.shape
+            if isinstance(s, tuple) and len(s) == rank:
+                return a
+    return None
+
+
+# ----------------------------------------------------------------------------- sdpa
+def _match_sdpa(t: _Trace, args: tuple) -> Optional[Binding]:
+    if len(t.b.args) != 4 or not t.has("exp", "fmax"):
+        return None
+    dtype = t.b.args[0][2]
+    if dtype not in ("float", "bfloat"):
+        return None
+    if t.has("simd_sum", "dot", "threadgroup_alloc"):
+        # GQA decode attention over an interleaved [kv_head, token, K|V] buffer,
+        # no 1/sqrt(D) scale, running max initialised from buffer 2.
+        return Binding("sdpa", dtype, {"scale": 1.0, "causal": False}, layout="gqa_interleaved")
+    if t.has("dot") and t.kinds["scf_for"] >= 1:
+        widths = t.vec_widths()
+        d = widths[0] if widths else None
+        scale = None
+        for op in t.ops:
+            if op.op == "rsqrt":
+                c = t.const_of(op.operands[0])
+                if c:
+                    scale = 1.0 / math.sqrt(c)
+        params = {"scale": scale if scale is not None else 1.0, "causal": False}
+        if d:
+            params["head_dim"] = d
+        q = _first_tensor(args, 2)
+        if q is not None:
+            params["seq_q"] = q.layout.shape[0]
+            params["head_dim"] = q.layout.shape[1]
+        return Binding("sdpa", dtype, params, layout="rows")
+    return None
+
+
+# ----------------------------------------------------------------------------- gemm
+def _match_gemm(t: _Trace, args: tuple) -> Optional[Binding]:
+    if len(t.b.args) != 3:
+        return None
+    dtype = t.b.args[0][2]
+    if t.has("async_copy_2d_d2t"):
+        uints = [c for c in t.consts("uint") if isinstance(c, int)]
+        # The example names K and the B/C row pitch with metal_cast(..., "uint").
+        ops2d = [op for op in t.ops if op.op == "async_copy_2d_d2t"]
+        k = t.const_of(ops2d[0].operands[3]) if ops2d else None
+        n = t.const_of(ops2d[1].operands[3]) if len(ops2d) > 1 else None
+        params = {}
+        if k:
+            params["K"] = int(k)
+        if n:
+            params["N"] = int(n)
+        params["tile_consts"] = sorted(set(uints))[:8]
+        return Binding("gemm", dtype, params, layout="async_tiles")
+    if t.has("dot", "make_vec") and not t.kinds["exp"]:
+        widths = t.vec_widths()
+        if not widths or len(set(widths)) != 1:
+            return None
+        k = widths[0]
+        c_name = t.b.args[2][0]
+        reads_c = any(op.op == "load" and op.attrs.get("buffer") == c_name for op in t.ops)
+        params = {"K": k, "accumulate": bool(reads_c)}
+        # the row pitch of B / C is the uint constant the kernel names `n`
+        ncands = [c for c in t.consts("uint") if isinstance(c, int) and c > 3 and c != k]
+        if ncands:
+            params["N"] = ncands[0]
+        return Binding("gemm", dtype, params, layout="dense")
+    return None
+
+
+# ----------------------------------------------------------------------------- decode layer
+def _match_decode(t: _Trace, args: tuple) -> Optional[Binding]:
+    if len(t.b.args) < 20 or not t.has("rsqrt", "exp", "simd_sum"):
+        return None
+    from .. import decode_layer
+    return decode_layer.bind_from_trace(t)
+
+
+_MATCHERS = (_match_decode, _match_rmsnorm, _match_sdpa, _match_gemm)
+
+
+def recognize(builder: KernelBuilder, args: tuple = ()) -> Binding:
+    t = _Trace(builder)
+    for m in _MATCHERS:
+        b = m(t, args)
+        if b is not None:
+            return b
+    raise EnigmaError(
+        f"no sm_100a implementation for kernel '{builder.kernel_name}': the B200 backend runs "
+        f"the hot-path operators (RMSNorm, SDPA, GEMM, the Qwen decode layer) and has no "
+        f"general code generator or CPU fallback")

@@ -109,6 +109,16 @@ int32_t enigma_sdpa_f32(const void* Q, const void* K, const void* V, void* O, in
                         int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
                         int64_t head_dim, float scale, int32_t causal, void* stream);
 
+/* Attention over strided views (CUDA cores, any head_dim <= 256): strides12 holds the
+ * element strides (batch, head, sequence) of Q, K, V and O in that order; head_dim is
+ * contiguous.  Lets reference layouts run without copies, e.g. the token-major Q/O
+ * [tokens, heads, D] and the interleaved [kv_head, token, K|V] buffer of
+ * examples/benchmark_sdpa.py:188-194. */
+int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const void* V, void* O,
+                            int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
+                            int64_t seq_kv, int64_t head_dim, const int64_t* strides12,
+                            float scale, int32_t causal, void* stream);
+
 /* ---- generic dispatch by kernel id: replaces enigma_dispatch /
  *      enigma_dispatch_timed (libenigma_runtime.swift:132-214).
  *      grid / threads are Metal-style totals (threads per axis, not groups),
