@@ -1,0 +1,122 @@
+"""Turn a recognizer Binding plus the bound buffers into one C-ABI call.
+
+The Metal kernels read their extents from the buffers they are bound to and
+from compile-time constants; the same information resolves the sizes here:
+buffer byte counts (in bind order), the Metal-style grid (total threads per
+axis) and the trace's constants.  Every plan is validated before anything is
+launched and raises RuntimeError with the kernel's context otherwise.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Callable, List, Sequence, Tuple
+
+from .. import _native
+
+_ES = {"float": 4, "bfloat": 2}
+_DT = {"float": _native.DTYPE_F32, "bfloat": _native.DTYPE_BF16}
+
+
+@dataclass
+class LaunchPlan:
+    """A ready C-ABI call: fn(pointers, stream) enqueues the kernel."""
+
+    describe: str
+    fn: Callable[[Sequence[int], int], None]
+    outputs: Tuple[int, ...]          # bind slots written by the kernel
+
+
+def _need(cond: bool, msg: str):
+    if not cond:
+        raise RuntimeError(f"enigma GPU error: {msg}")
+
+
+def _div(nbytes: int, per: int, what: str) -> int:
+    _need(per > 0 and nbytes % per == 0,
+          f"{what}: buffer of {nbytes} bytes is not a whole number of {per}-byte units")
+    return nbytes // per
+
+
+def plan(binding, nbytes: List[int], grid: Tuple[int, ...], threads: Tuple[int, ...]) -> LaunchPlan:
+    op = binding.op
+    if op == "rmsnorm":
+        return _plan_rmsnorm(binding, nbytes)
+    if op == "gemm":
+        return _plan_gemm(binding, nbytes)
+    if op == "sdpa":
+        return _plan_sdpa(binding, nbytes, grid, threads)
+    if op == "decode":
+        from ..decode_layer import plan_decode
+        return plan_decode(binding, nbytes)
+    raise RuntimeError(f"enigma GPU error: no launch plan for operator {op!r}")
+
+
+def _plan_rmsnorm(b, nbytes):
+    _need(len(nbytes) == 3, f"rmsnorm binds 3 buffers (x, w, y), got {len(nbytes)}")
+    es = _ES[b.dtype]
+    hidden = int(b.params.get("hidden") or _div(nbytes[1], es, "rmsnorm w"))
+    rows = _div(nbytes[0], es * hidden, "rmsnorm x")
+    _need(nbytes[2] >= rows * hidden * es, "rmsnorm: output buffer smaller than x")
+    _need(nbytes[1] >= hidden * es, "rmsnorm: weight buffer smaller than hidden")
+    eps, dt = float(b.params["eps"]), _DT[b.dtype]
+
+    def fn(p, stream):
+        _native.call("enigma_rmsnorm", dt, p[0], p[1], p[2], rows, hidden, ctypes.c_float(eps),
+                     stream)
+    return LaunchPlan(f"rmsnorm rows={rows} hidden={hidden} eps={eps}", fn, (2,))
+
+
+def _plan_gemm(b, nbytes):
+    _need(len(nbytes) == 3, f"gemm binds 3 buffers (A, B, C), got {len(nbytes)}")
+    es = _ES[b.dtype]
+    k = int(b.params["K"])
+    m = _div(nbytes[0], es * k, "gemm A")
+    n = int(b.params.get("N") or _div(nbytes[1], es * k, "gemm B"))
+    _need(nbytes[1] >= k * n * es, f"gemm: B holds {nbytes[1]} bytes, needs K*N = {k}x{n}")
+    _need(nbytes[2] >= m * n * es, f"gemm: C holds {nbytes[2]} bytes, needs M*N = {m}x{n}")
+    acc = bool(b.params.get("accumulate", False))
+    if b.dtype == "bfloat":
+        _need(not acc, "gemm: C += A B is fp32-only")
+
+        def fn(p, stream):
+            _native.call("enigma_gemm_bf16", p[0], p[1], p[2], m, n, k, stream)
+    else:
+        def fn(p, stream):
+            _native.call("enigma_gemm_f32", p[0], p[1], p[2], m, n, k, int(acc), stream)
+    return LaunchPlan(f"gemm M={m} N={n} K={k} accumulate={acc}", fn, (2,))
+
+
+def _plan_sdpa(b, nbytes, grid, threads):
+    _need(len(nbytes) == 4, f"attention binds 4 buffers, got {len(nbytes)}")
+    es, dt = _ES[b.dtype], _DT[b.dtype]
+    scale = float(b.params.get("scale", 1.0))
+    causal = int(bool(b.params.get("causal", False)))
+    if b.layout == "gqa_interleaved":
+        # Q, O: [tokens, Hq, D]; KV: [Hkv, kv_tokens, 2D] (K then V); buffer 2: Hq floats
+        # (the running max start value, -1e30 in the example, so it never binds).
+        hq = _div(nbytes[2], 4, "running-max buffer")
+        hkv = int(grid[1])
+        tokens = int(grid[0]) // int(threads[0])
+        _need(tokens > 0 and hkv > 0 and hq % hkv == 0,
+              f"grid {grid} / threads {threads} do not give tokens and kv heads")
+        d = _div(nbytes[0], es * tokens * hq, "attention Q")
+        kv_tokens = _div(nbytes[1], es * hkv * 2 * d, "attention KV")
+        strides = (ctypes.c_int64 * 12)(0, d, hq * d, 0, kv_tokens * 2 * d, 2 * d,
+                                        0, kv_tokens * 2 * d, 2 * d, 0, d, hq * d)
+
+        def fn(p, stream):
+            _native.call("enigma_sdpa_strided", dt, p[0], p[1], p[1] + d * es, p[3], 1, hq, hkv,
+                         tokens, kv_tokens, d, strides, ctypes.c_float(scale), causal, stream)
+        return LaunchPlan(f"sdpa gqa tokens={tokens} Hq={hq} Hkv={hkv} D={d} "
+                          f"kv_tokens={kv_tokens}", fn, (3,))
+    d = int(b.params["head_dim"])
+    sq = _div(nbytes[0], es * d, "attention Q")
+    sk = _div(nbytes[1], es * d, "attention K")
+    _need(nbytes[2] >= sk * d * es and nbytes[3] >= sq * d * es, "attention V / O too small")
+    name = "enigma_sdpa_bf16" if b.dtype == "bfloat" else "enigma_sdpa_f32"
+
+    def fn(p, stream):
+        _native.call(name, p[0], p[1], p[2], p[3], 1, 1, 1, sq, sk, d, ctypes.c_float(scale),
+                     causal, stream)
+    return LaunchPlan(f"sdpa rows Sq={sq} Sk={sk} D={d} scale={scale}", fn, (3,))
