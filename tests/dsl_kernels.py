@@ -1,0 +1,221 @@
+"""Enigma DSL kernels written the way the reference's callers write them.
+
+Each follows the algorithm of one reference example or test kernel (cited),
+expressed against this package's public API.  The tests compile them with
+enigma.compile, check what the recognizer bound, and (on a GPU) run them
+through MetalRuntime.execute against the CPU oracle.
+"""
+import enigma
+from enigma.tensor import Tensor, tensor_composition, tensor_zipped_divide
+
+
+# ---------------------------------------------------------------- RMSNorm (TV layout)
+# examples/benchmark_rmsnorm.py:31-84: one threadgroup per row, a TV layout of
+# `threads` x `values`, simd_sum -> threadgroup scratch -> simd_sum, rsqrt.
+def make_rmsnorm(rows, n, threads, values, eps, dtype="float"):
+    tiler, tv = enigma.make_layout_tv(enigma.make_ordered_layout((threads,), order=(0,)),
+                                      enigma.make_ordered_layout((values,), order=(0,)))
+
+    @enigma.kernel
+    def rmsnorm_kernel(gX, gW, gOut, tv_layout, tiler_mn):
+        tidx, _, _ = enigma.arch.thread_idx()
+        row, _, _ = enigma.arch.block_idx()
+        x_row = gX[((None, None), row)][(0, None)]
+        y_row = gOut[((None, None), row)][(0, None)]
+        w_all = gW[(None,)]
+        mine_x = tensor_composition(x_row, tv_layout, tiler_mn)[(tidx, None)]
+        mine_y = tensor_composition(y_row, tv_layout, tiler_mn)[(tidx, None)]
+        mine_w = tensor_composition(w_all, tv_layout, tiler_mn)[(tidx, None)]
+        xv = mine_x.load()
+        wv = mine_w.load()
+        part = enigma.simd_sum(xv * xv)
+        scratch = enigma.threadgroup_alloc("float", 32)
+        lane = enigma.thread_index_in_simdgroup()
+        warp = enigma.simdgroup_index_in_threadgroup()
+        enigma.store_if(scratch, warp, part, enigma.cmp_eq(lane, 0))
+        enigma.barrier()
+        v = enigma.load_if(scratch, lane, enigma.cmp_ult(lane, enigma.simdgroups_per_threadgroup()),
+                           default=0.0)
+        total = enigma.simd_sum(v)
+        inv = enigma.rsqrt(total / float(n) + eps)
+        mine_y.store(xv * inv * wv)
+
+    @enigma.jit
+    def rmsnorm_jit(mX, mW, mOut):
+        gX = tensor_zipped_divide(mX, (1, tiler[0]))
+        gOut = tensor_zipped_divide(mOut, (1, tiler[0]))
+        gW = tensor_zipped_divide(mW, tiler)
+        t = enigma.size(tv, mode=[0])
+        rmsnorm_kernel(gX, gW, gOut, tv, tiler).launch(grid=(rows * t, 1, 1), block=(t, 1, 1))
+
+    mX = Tensor("X", 0, dtype, enigma.Layout((rows, n), (n, 1)))
+    mW = Tensor("W", 1, dtype, enigma.Layout((n,), (1,)))
+    mOut = Tensor("Out", 2, dtype, enigma.Layout((rows, n), (n, 1)))
+    return rmsnorm_jit, (mX, mW, mOut)
+
+
+# ---------------------------------------------------------------- GQA decode attention
+# examples/benchmark_sdpa.py:48-158: threadgroup per (token, kv head), QMUL q heads
+# per kv head, simdgroups stride the KV tokens, online softmax, cross-simdgroup merge.
+def make_sdpa_gqa(tokens, q_heads, kv_heads, head_dim, kv_tokens, n_sg=4):
+    qmul = q_heads // kv_heads
+    thr = n_sg * 32
+    tiler_d, tv_d = enigma.make_layout_tv(enigma.make_ordered_layout((32,), order=(0,)),
+                                          enigma.make_ordered_layout((2,), order=(0,)))
+
+    def head_vec(base, lane):
+        t = Tensor("Q", 0, "float", enigma.Layout(head_dim, 1), base_offset=base)
+        tiled = tensor_zipped_divide(t, tiler_d)
+        return tensor_composition(tiled[(None,)], tv_d, tiler_d)[(lane, None)].load()
+
+    @enigma.kernel
+    def sdpa_gqa(mQ, mKV, mM0, mO):
+        qt = enigma.threadgroup_position_in_grid("x")
+        h = enigma.threadgroup_position_in_grid("y")
+        lane = enigma.thread_index_in_simdgroup()
+        sg = enigma.simdgroup_index_in_threadgroup()
+        q = [head_vec(qt * (q_heads * head_dim) + h * (qmul * head_dim) + g * head_dim, lane)
+             for g in enigma.range_constexpr(qmul)]
+        m = [mM0[h * qmul + g] for g in enigma.range_constexpr(qmul)]
+        l = [enigma.where(enigma.metal_cast(0.0, "float"), enigma.metal_cast(1.0, "float"),
+                          enigma.cmp_eq(sg, 0)) for _ in range(qmul)]
+        ox = [enigma.metal_cast(0.0, "float") for _ in range(qmul)]
+        oy = [enigma.metal_cast(0.0, "float") for _ in range(qmul)]
+        for it in enigma.range(kv_tokens // n_sg):
+            base = h * kv_tokens * 2 * head_dim + (it * n_sg + sg) * 2 * head_dim
+            kv = enigma.make_float2(mKV[base + lane * 2], mKV[base + lane * 2 + 1])
+            vx = mKV[base + head_dim + lane * 2]
+            vy = mKV[base + head_dim + lane * 2 + 1]
+            for g in enigma.range_constexpr(qmul):
+                s = enigma.simd_sum(enigma.dot(q[g], kv))
+                mn = enigma.fmax(m[g], s)
+                a = enigma.exp(m[g] - mn)
+                p = enigma.exp(s - mn)
+                l[g] = enigma.fma(l[g], a, p)
+                m[g] = mn
+                ox[g] = enigma.fma(vx, p, ox[g] * a)
+                oy[g] = enigma.fma(vy, p, oy[g] * a)
+        shared = enigma.threadgroup_alloc("float", 2 * qmul * n_sg)
+        for g in enigma.range_constexpr(qmul):
+            enigma.store_if(shared, g * n_sg + sg, m[g], enigma.cmp_eq(lane, 0))
+        enigma.barrier()
+        for g in enigma.range_constexpr(qmul):
+            out = ox[g] / l[g]
+            mO[qt * q_heads * head_dim + h * qmul * head_dim + g * head_dim + lane * 2] = out
+            mO[qt * q_heads * head_dim + h * qmul * head_dim + g * head_dim + lane * 2 + 1] = \
+                oy[g] / l[g]
+
+    @enigma.jit
+    def sdpa_jit(mQ, mKV, mM0, mO):
+        sdpa_gqa(mQ, mKV, mM0, mO).launch(grid=(tokens * thr, kv_heads, 1), block=(thr, 1, 1))
+
+    args = (Tensor("Q", 0, "float", enigma.Layout(tokens * q_heads * head_dim, 1)),
+            Tensor("KV", 1, "float", enigma.Layout(kv_heads * kv_tokens * 2 * head_dim, 1)),
+            Tensor("M0", 2, "float", enigma.Layout(q_heads, 1)),
+            Tensor("O", 3, "float", enigma.Layout(tokens * q_heads * head_dim, 1)))
+    return sdpa_jit, args, thr
+
+
+# ---------------------------------------------------------------- FlashAttention-1 rows
+# examples/showcase_attention.py:31-91: one thread per query row, KV tiles of BC keys,
+# carried (m, l, o[0..3]) with 1/sqrt(D) scaling; D = 4.
+def make_fa(n_keys, bc=16):
+    D = 4
+    nt = n_keys // bc
+
+    def body(Q, K, V, O, row):
+        d = enigma.metal_cast(D, "uint")
+        qb = row * d
+        qv = enigma.make_float4(Q[qb], Q[qb + 1], Q[qb + 2], Q[qb + 3])
+        sc = enigma.rsqrt(enigma.metal_cast(D, "float"))
+        neg = enigma.metal_cast(-1e30, "float")
+        z = enigma.metal_cast(0, "float")
+        with enigma.for_range(0, enigma.metal_cast(nt, "int"), init=[neg, z, z, z, z, z]) as (t, c):
+            tb = enigma.metal_cast(t, "uint") * enigma.metal_cast(bc, "uint") * d
+            s = []
+            for j in range(bc):
+                kb = tb + enigma.metal_cast(j * D, "uint")
+                s.append(enigma.dot(qv, enigma.make_float4(K[kb], K[kb + 1], K[kb + 2],
+                                                           K[kb + 3])) * sc)
+            mt = s[0]
+            for x in s[1:]:
+                mt = enigma.fmax(mt, x)
+            mn = enigma.fmax(c[0], mt)
+            a = enigma.exp(c[0] - mn)
+            ps = [enigma.exp(x - mn) for x in s]
+            tot = ps[0]
+            for p in ps[1:]:
+                tot = tot + p
+            o = [a * c[2 + i] for i in range(4)]
+            for j in range(bc):
+                vb = tb + enigma.metal_cast(j * D, "uint")
+                o = [enigma.fma(ps[j], V[vb + i], o[i]) for i in range(4)]
+            c[1] = a * c[1] + tot
+            c[0] = mn
+            for i in range(4):
+                c[2 + i] = o[i]
+        inv = enigma.metal_cast(1, "float") / c[1]
+        for i in range(4):
+            O[row * d + i] = c[2 + i] * inv
+
+    @enigma.kernel
+    def fa_naive(Q: enigma.f32, K: enigma.f32, V: enigma.f32, O: enigma.f32):
+        body(Q, K, V, O, enigma.thread_position_in_grid)
+
+    return fa_naive
+
+
+# ---------------------------------------------------------------- K = 4 matmul / gemm
+# tests/metal/test_gemm_matmul_runtime.py:20-60
+def make_k4(n_cols, accumulate):
+    def body(A, B, C):
+        row = enigma.thread_position_in_grid_xyz("y")
+        col = enigma.thread_position_in_grid_xyz("x")
+        n = enigma.metal_cast(n_cols, "uint")
+        k = enigma.metal_cast(4, "uint")
+        av = enigma.make_float4(*[A[row * k + i] for i in range(4)])
+        bv = enigma.make_float4(*[B[col + n * i] for i in range(4)])
+        idx = row * n + col
+        C[idx] = enigma.dot(av, bv) + C[idx] if accumulate else enigma.dot(av, bv)
+
+    if accumulate:
+        @enigma.kernel
+        def gemm_k4(A: enigma.f32, B: enigma.f32, C: enigma.f32):
+            body(A, B, C)
+        return gemm_k4
+
+    @enigma.kernel
+    def matmul_k4(A: enigma.f32, B: enigma.f32, C: enigma.f32):
+        body(A, B, C)
+    return matmul_k4
+
+
+# ---------------------------------------------------------------- async-copy tiled GEMM
+# examples/async_copy_gemm.py:32-79: A/B tiles staged into threadgroup memory with 2-D
+# async copies, K loop over tiles.
+def make_async_gemm(m, n, k, tm=32, tn=32, tk=16):
+    @enigma.kernel
+    def gemm_async(A: enigma.f32, B: enigma.f32, C: enigma.f32):
+        tg = enigma.threadgroup_position_in_grid()
+        cols = enigma.metal_cast(n // tn, "uint")
+        bx, by = tg / cols, tg % cols
+        sg = enigma.simdgroup_index_in_threadgroup()
+        a_tile = enigma.threadgroup_alloc("float", tm * tk)
+        b_tile = enigma.threadgroup_alloc("float", tk * tn)
+        acc = enigma.register_tensor((2, 2), dtype="float", fill=0.0)
+        zero = enigma.metal_cast(0, "uint")
+        kc = enigma.metal_cast(k, "uint")
+        nc = enigma.metal_cast(n, "uint")
+        for kt in range(k // tk):
+            koff = enigma.metal_cast(kt, "uint") * enigma.metal_cast(tk, "uint")
+            with enigma.if_(enigma.cmp_eq(sg, 0)) as (then_b, _):
+                with then_b:
+                    ea = enigma.async_copy_2d_d2t(a_tile, zero, tk, A, bx * tm * kc + koff, kc,
+                                                  tk, tm)
+                    eb = enigma.async_copy_2d_d2t(b_tile, zero, tn, B, koff * nc + by * tn, nc,
+                                                  tn, tk)
+                    enigma.async_copy_wait(ea, eb)
+            enigma.barrier()
+        C[(bx * tm) * nc + by * tn + enigma.thread_position_in_threadgroup()] = acc[0, 0]
+
+    return gemm_async

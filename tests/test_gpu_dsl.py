@@ -1,0 +1,127 @@
+"""End to end through the reference-facing API on the GPU:
+enigma.compile -> MetalRuntime.execute / prepare -> sm_100a kernel, checked
+against the CPU oracle with the same tolerances as the example scripts
+(benchmark_rmsnorm.py:127-136, benchmark_sdpa.py:220-232,
+showcase_attention.py:159-170, test_gemm_matmul_runtime.py:136,166) or tighter."""
+import numpy as np
+import pytest
+
+import enigma
+import dsl_kernels as K
+from oracle import numerics as orc
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rt(cuda):
+    return enigma.MetalRuntime()
+
+
+def test_rmsnorm_config1(rt):
+    rows = n = 4096
+    jit, args = K.make_rmsnorm(rows, n, 256, 4, 1e-6)
+    ck = enigma.compile(jit, *args)
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((rows, n), dtype=np.float32)
+    w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    raw = rt.execute(ck, [x.ravel(), w], rows * n * 4, grid=ck.grid, threads=ck.block)
+    y = np.frombuffer(raw, np.float32).reshape(rows, n)
+    np.testing.assert_allclose(y, orc.rmsnorm(x, w, 1e-6), rtol=1e-5, atol=1e-6)
+
+
+def test_rmsnorm_prepare_timed(rt):
+    jit, args = K.make_rmsnorm(512, 4096, 256, 16, 1e-5)
+    ck = enigma.compile(jit, *args)
+    rng = np.random.default_rng(42)
+    x = rng.standard_normal((512, 4096), dtype=np.float32)
+    w = rng.standard_normal(4096).astype(np.float32)
+    prep = rt.prepare(ck, [x.ravel(), w], 512 * 4096 * 4)
+    try:
+        for _ in range(3):
+            prep.dispatch(ck.grid, ck.block)
+        us = prep.dispatch_timed(ck.grid, ck.block)
+        assert 0 < us < 1e5
+        r = enigma.benchmark.bench_gpu(prep, ck.grid, ck.block, repeat=5, warmup=1)
+        assert r.median_us > 0
+        y = np.frombuffer(prep.read_output(), np.float32).reshape(512, 4096)
+        np.testing.assert_allclose(y, orc.rmsnorm(x, w, 1e-5), rtol=1e-5, atol=1e-6)
+    finally:
+        prep.release()
+
+
+def test_sdpa_gqa_reference_shape(rt):
+    """benchmark_sdpa.py shape: 128 tokens, 64 q heads / 8 kv heads, d 64, 512 kv tokens,
+    interleaved KV, no scale, running max buffer = -1e30."""
+    T, H, G, D, S = 128, 64, 8, 64, 512
+    jit, args, thr = K.make_sdpa_gqa(T, H, G, D, S)
+    ck = enigma.compile(jit, *args)
+    rng = np.random.default_rng(42)
+    q = (rng.standard_normal((T, H, D)) * 0.1).astype(np.float32)
+    k = (rng.standard_normal((G, S, D)) * 0.1).astype(np.float32)
+    v = (rng.standard_normal((G, S, D)) * 0.1).astype(np.float32)
+    kv = np.concatenate([k, v], axis=2)
+    m0 = np.full(H, -1e30, np.float32)
+    raw = rt.execute(ck, [q.ravel(), kv.ravel(), m0], T * H * D * 4, grid=ck.grid,
+                     threads=ck.block)
+    o = np.frombuffer(raw, np.float32).reshape(T, H, D)
+    ref = orc.sdpa(q.transpose(1, 0, 2)[None], k[None], v[None], 1.0)[0].transpose(1, 0, 2)
+    np.testing.assert_allclose(o, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_fa_d4(rt):
+    ck = enigma.compile(K.make_fa(1024))
+    rng = np.random.default_rng(1234)
+    q, k, v = (rng.standard_normal((1024, 4)).astype(np.float32) for _ in range(3))
+    raw = rt.execute(ck, [q.ravel(), k.ravel(), v.ravel()], 1024 * 4 * 4, grid=(1024, 1, 1),
+                     threads=(32, 1, 1))
+    o = np.frombuffer(raw, np.float32).reshape(1024, 4)
+    np.testing.assert_allclose(o, orc.sdpa(q[None, None], k[None, None], v[None, None], 0.5)[0, 0],
+                               rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("acc", [False, True])
+@pytest.mark.parametrize("m", [4, 32, 128])
+def test_k4(rt, m, acc):
+    ck = enigma.compile(K.make_k4(64, acc))
+    rng = np.random.default_rng(m)
+    a = rng.standard_normal((m, 4)).astype(np.float32)
+    b = rng.standard_normal((4, 64)).astype(np.float32)
+    raw = rt.execute(ck, [a.ravel(), b.ravel()], m * 64 * 4, grid=(64, m, 1),
+                     threads=(16, min(m, 16), 1))
+    np.testing.assert_allclose(np.frombuffer(raw, np.float32).reshape(m, 64), a @ b,
+                               rtol=1e-4, atol=1e-4)
+
+
+def test_async_gemm(rt):
+    ck = enigma.compile(K.make_async_gemm(64, 64, 64))
+    rng = np.random.default_rng(0)
+    a = (rng.standard_normal((64, 64)) * 0.1).astype(np.float32)
+    b = (rng.standard_normal((64, 64)) * 0.1).astype(np.float32)
+    raw = rt.execute(ck, [a.ravel(), b.ravel()], 64 * 64 * 4, grid=(4, 1, 1), threads=(128, 1, 1))
+    np.testing.assert_allclose(np.frombuffer(raw, np.float32).reshape(64, 64), a @ b,
+                               rtol=1e-4, atol=1e-5)
+
+
+def test_torch_zero_copy_and_torch_outputs(rt):
+    import torch
+    jit, args = K.make_rmsnorm(64, 2048, 256, 8, 1e-6, dtype="bfloat")
+    ck = enigma.compile(jit, *args)
+    x = torch.randn(64, 2048, device="cuda").bfloat16()
+    w = torch.ones(2048, device="cuda").bfloat16()
+    y = rt.execute(ck, [x, w], None, grid=ck.grid, threads=ck.block,
+                   output_shapes=[(64, 2048)], output_dtypes=[torch.bfloat16])
+    ref = orc.rmsnorm(x.float().cpu().numpy(), w.float().cpu().numpy(), 1e-6)
+    got = y.float().cpu().numpy()
+    assert np.all(np.abs(got - ref) <= np.abs(ref) * 2.0 ** -7 + 1e-6)
+
+
+def test_bind_count_error(rt):
+    ck = enigma.compile(K.make_k4(64, False))
+    with pytest.raises(RuntimeError, match="Outputs are appended AFTER inputs"):
+        rt.execute(ck, [np.zeros(16, np.float32)], 64, grid=(1, 1, 1), threads=(1, 1, 1))
+
+
+def test_device_capabilities(rt):
+    caps = rt.device_capabilities()
+    assert caps.gpu_family == "sm_100" and caps.sm_count >= 100 and caps.simdgroup_size == 32

@@ -1,0 +1,69 @@
+"""compile() -> recognizer bindings for the hot-path kernels (CPU only)."""
+import pytest
+
+import enigma
+import dsl_kernels as K
+
+
+def test_rmsnorm_binding_config1():
+    jit, args = K.make_rmsnorm(4096, 4096, 256, 4, 1e-6)
+    ck = enigma.compile(jit, *args)
+    b = ck.cuda_kernel
+    assert b.op == "rmsnorm" and b.dtype == "float"
+    assert b.params["eps"] == pytest.approx(1e-6) and b.params["hidden"] == 4096
+    assert b.params["rows"] == 4096 and b.params["vector_run"] == 4
+    assert ck.grid == (4096 * 256, 1, 1) and ck.block == (256, 1, 1)
+    assert ck.num_params == 3 and ck.param_names == ["X", "W", "Out"]
+
+
+def test_rmsnorm_binding_bf16_vec8():
+    jit, args = K.make_rmsnorm(64, 8192, 256, 8, 1e-5, dtype="bfloat")
+    b = enigma.compile(jit, *args).cuda_kernel
+    assert (b.op, b.dtype, b.params["vector_run"]) == ("rmsnorm", "bfloat", 8)
+    assert b.params["eps"] == pytest.approx(1e-5)
+
+
+def test_sdpa_gqa_binding():
+    jit, args, thr = K.make_sdpa_gqa(16, 16, 2, 64, 64)
+    ck = enigma.compile(jit, *args)
+    assert ck.cuda_kernel.op == "sdpa" and ck.cuda_kernel.layout == "gqa_interleaved"
+    assert ck.grid == (16 * thr, 2, 1)
+
+
+def test_fa_binding():
+    ck = enigma.compile(K.make_fa(1024))
+    b = ck.cuda_kernel
+    assert (b.op, b.layout, b.params["head_dim"]) == ("sdpa", "rows", 4)
+    assert b.params["scale"] == pytest.approx(0.5)
+
+
+@pytest.mark.parametrize("acc", [False, True])
+def test_k4_binding(acc):
+    b = enigma.compile(K.make_k4(64, acc)).cuda_kernel
+    assert (b.op, b.params["K"], b.params["N"], b.params["accumulate"]) == ("gemm", 4, 64, acc)
+
+
+def test_async_gemm_binding():
+    b = enigma.compile(K.make_async_gemm(64, 64, 64)).cuda_kernel
+    assert (b.op, b.layout, b.params["K"], b.params["N"]) == ("gemm", "async_tiles", 64, 64)
+
+
+def test_unrecognised_kernel_raises():
+    @enigma.kernel
+    def add(A: enigma.f32, B: enigma.f32, C: enigma.f32):
+        i = enigma.thread_position_in_grid
+        C[i] = A[i] + B[i]
+
+    with pytest.raises(enigma.EnigmaError, match="no sm_100a implementation"):
+        enigma.compile(add)
+
+
+def test_launch_outside_compile_raises():
+    jit, args = K.make_rmsnorm(8, 1024, 256, 4, 1e-6)
+    with pytest.raises(RuntimeError, match="outside enigma.compile"):
+        jit.fn(*args)
+
+
+def test_tracing_records_loops_and_carries():
+    ck = enigma.compile(K.make_fa(64))
+    assert "scf_for" in ck.metal_source and "exp" in ck.metal_source
