@@ -54,4 +54,4 @@ def test_merge_scalars():
     out = _merge_scalar_buffers([a, b], [7], [("n", 1, "uint")], num_outputs=1)
     assert out[0] is a and out[2] is b and out[1].dtype == np.uint32 and out[1][0] == 7
     with pytest.raises(RuntimeError, match="output region"):
-        _merge_scalar_buffers([a], [7], [("n", 1, "uint")], num_outputs=1)
+        _merge_scalar_buffers([a], [7], [("n", 2, "uint")], num_outputs=1)
