@@ -345,21 +345,56 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_single_op(args):
+    """One operator alone at a chosen size (profiling cases for ncu; not the headline)."""
+    import torch
+    from enigma import cuda_ops
+    cuda_ops.ensure_device(0)
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    n = args.size
+    if args.only == "gemm":
+        a = (torch.randn(n, n, device="cuda", generator=g) / math.sqrt(n)).bfloat16()
+        b = torch.randn(n, n, device="cuda", generator=g).bfloat16()
+        c = torch.empty_like(a)
+        fn, work, unit = (lambda: cuda_ops.gemm(a, b, out=c)), 2 * n ** 3, "TFLOP/s"
+    else:
+        B, H, D = 8, 32, 128
+        q, k, v = (torch.randn(B, H, n, D, device="cuda", generator=g).bfloat16()
+                   for _ in range(3))
+        o = torch.empty_like(q)
+        causal = args.only == "sdpa_causal"
+        fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
+        work, unit = (2 if causal else 4) * B * H * n * n * D, "TFLOP/s"
+    for _ in range(args.warmup):
+        fn()
+    ms = _time_device(fn, args.steps, stream)
+    cuda_ops.synchronize(0)
+    print(json.dumps({"op": args.only, "size": n, "ms": round(ms, 4),
+                      "value": round(work / (ms * 1e-3) / 1e12, 1), "unit": unit}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the GEMM/SDPA side numbers")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--cpu-rows", type=int, default=16384)
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (smaller cases are for profiling only)")
+    ap.add_argument("--only", choices=["gemm", "sdpa", "sdpa_causal"], default=None,
+                    help="time one operator alone (profiling case)")
+    ap.add_argument("--size", type=int, default=4096, help="--only: n for GEMM n^3, S for SDPA")
     args = ap.parse_args()
     _set_rows(args.rows)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.only:
+        run_single_op(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
