@@ -41,8 +41,8 @@ ROWS, HIDDEN, EPS = 262144, 8192, 1e-6
 METRIC = "RMSNorm HBM GB/s (bf16 262144x8192, fp32 accumulate)"
 BYTES_PER_STEP = 4 * ROWS * HIDDEN + 2 * HIDDEN
 # DRAM bytes (read + write) of one rmsnorm launch at this size, from the ncu
-# capture summarised in profiles/rmsnorm_bf16_262144x8192.md (None until captured).
-NCU_TRAFFIC_PER_LAUNCH = None
+# capture summarised in profiles/rmsnorm_bf16_262144x8192.md (small case scaled x8).
+NCU_TRAFFIC_PER_LAUNCH = 8_192_407_552
 
 
 def _set_rows(rows: int) -> None:
