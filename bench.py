@@ -224,7 +224,30 @@ def _ops_side(hbm_peak, tc_peak, peak_kind):
             res[f"sdpa_bf16_{'causal' if causal else 'noncausal'}_8x32x8192x128"] = {
                 "tflops": round(tf, 1), "ms": round(ms, 3), "frac": round(tf / tc_peak, 4),
                 "flops_convention": "causal 2*B*H*S^2*D, non-causal 4*B*H*S^2*D"}
+    res["decode_layer_config5"] = _decode_side(hbm_peak)
     return res
+
+
+def _decode_side(hbm_peak):
+    """one decode step, batch 64, 2048-token KV cache (HBM-bound)."""
+    import torch
+    from enigma.decode_layer import DecodeConfig, DecodeLayer
+    cfg = DecodeConfig()
+    layer = DecodeLayer.random(cfg, seed=0)
+    x = torch.randn(cfg.batch, cfg.hidden, device="cuda").bfloat16()
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    fn = lambda: layer.step(x, out=out)  # noqa: E731
+    for _ in range(5):
+        fn()
+    ms = _time_device(fn, 50, stream)
+    kv = 2 * cfg.batch * cfg.heads_kv * (cfg.cache_len + 1) * cfg.head_dim * 2
+    byts = layer.weight_bytes() + kv
+    return {"ms": round(ms, 4), "tokens_per_s": round(cfg.batch / (ms * 1e-3), 1),
+            "algorithmic_bytes": byts, "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+            "frac_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+            "note": "weights + KV read once per step; L2 (126 MB) can hold part of the "
+                    "97 MB working set across repeated steps"}
 
 
 def _sdpa_tc_available() -> bool:

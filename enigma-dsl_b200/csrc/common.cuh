@@ -33,6 +33,10 @@ cudaError_t sdpa_bf16_launch(const void* Q, const void* K, const void* V, void* 
                              int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
                              float scale, bool causal, cudaStream_t s);
 
+size_t decode_workspace_bytes(const enigma_decode_layer_desc& d);
+cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x, void* out,
+                                void* ws, cudaStream_t s);
+
 // Records a message for enigma_last_error on the calling thread.
 void set_error(const char* fmt, ...);
 

@@ -1,0 +1,514 @@
+// decode.cu — one decoder-layer decode step (Qwen-style) on sm_100a.
+//
+// The reference runs the layer as one threadgroup-wide Metal megakernel
+// (examples/qwen_megakernel.py:228-269: RMSNorm -> Q/K/V matvec -> RoPE ->
+// SDPA over the KV cache -> O-proj + residual -> RMSNorm -> SwiGLU -> down-proj
+// + residual).  At batch 64 every GEMM is skinny (M = 64) and the step is bound
+// by HBM: ~30 MB of weights and ~67 MB of KV cache per step.  So:
+//
+//   * GEMMs are split-K tcgen05 kernels: grid (N/64 tiles, K splits) fills the
+//     148 SMs even for N = 896; each CTA streams its K range of B through a TMA
+//     ring and writes an fp32 128x64 partial tile to a workspace.
+//   * The split reduction is fused with what follows each GEMM: RoPE + KV-cache
+//     append (QKV), residual add + RMSNorm (O-proj), SwiGLU (gate/up), residual
+//     add (down-proj).
+//   * Attention is split-KV ("flash decoding"): CTAs of (sequence, kv head,
+//     key chunk) write (max, sum, o) partials for the group's query heads; a
+//     combine kernel merges the chunks.
+//
+// Workspace (caller-owned, enigma_decode_workspace_bytes) holds every partial
+// and intermediate, so a step makes no allocation.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace {
+
+using namespace enigma_sm100;
+
+// ============================================================================ split-K GEMM
+constexpr int SK_BM = 128;
+constexpr int SK_BN = 64;
+constexpr int SK_BK = 64;
+constexpr int SK_STAGES = 4;
+constexpr int SK_A_BYTES = SK_BM * SK_BK * 2;   // 16 KB
+constexpr int SK_B_BYTES = SK_BK * SK_BN * 2;   // 8 KB
+constexpr int SK_STAGE = SK_A_BYTES + SK_B_BYTES;
+constexpr int SK_SMEM = SK_STAGES * SK_STAGE + 1024 + 256;
+constexpr int SK_THREADS = 192;
+
+// partial[split][m][n] (fp32) = A[m, kslice] * B[kslice, n] for one 128 x 64 tile.
+// M <= 128 (rows past M are zero-filled by TMA and not stored).
+__global__ void __launch_bounds__(SK_THREADS)
+gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      float* __restrict__ partial, int M, int N, int K, int kb_per_split,
+                      uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + SK_STAGES * SK_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SK_STAGES * SK_STAGE);
+  uint64_t* empty = full + SK_STAGES;
+  uint64_t* acc_full = empty + SK_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = blockIdx.x, split = blockIdx.y;
+  const int num_kb = (K + SK_BK - 1) / SK_BK;
+  const int kb0 = split * kb_per_split;
+  const int kb1 = min(num_kb, kb0 + kb_per_split);
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < SK_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, SK_BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
+        const int s = i % SK_STAGES;
+        if (!mbar_wait(&empty[s], ((i / SK_STAGES) & 1) ^ 1, status)) break;
+        mbar_arrive_expect_tx(&full[s], SK_STAGE);
+        tma_load_2d(sA + s * SK_A_BYTES, &tmA, &full[s], kb * SK_BK, 0);
+        tma_load_2d(sB + s * SK_B_BYTES, &tmB, &full[s], nb * SK_BN, kb * SK_BK);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(SK_BM, SK_BN, false, true);
+      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+      bool ok = true;
+      for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
+        const int s = i % SK_STAGES;
+        if (!mbar_wait(&full[s], (i / SK_STAGES) & 1, status)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t da = smem_desc_sw128(a0 + s * SK_A_BYTES, 16, 1024);
+        const uint64_t db = smem_desc_sw128(b0 + s * SK_B_BYTES, SK_B_BYTES, 1024);
+#pragma unroll
+        for (int kk = 0; kk < SK_BK / 16; ++kk)
+          mma_bf16_ss(tmem, da + uint64_t((kk * 32) >> 4), db + uint64_t((kk * 2048) >> 4), idesc,
+                      (i | kk) != 0 ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      if (ok) mma_commit(acc_full);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const bool have = kb1 > kb0;
+    if (!have || mbar_wait(acc_full, 0, status)) {
+      tc_fence_after();
+      float* dst = partial + (int64_t(split) * M + row) * N + nb * SK_BN;
+      const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < SK_BN; c += 16) {
+        uint32_t r[16];
+        if (have) {
+          tmem_ld16(taddr + c, r);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) r[t] = 0u;
+        }
+        if (row < M && nb * SK_BN + c < N) {
+          float4* d4 = reinterpret_cast<float4*>(dst + c);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            d4[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, SK_BN);
+  }
+}
+
+// ============================================================================ reductions
+__device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
+
+// q / k / v = sum over splits of the QKV partials; RoPE on the q and k heads
+// (rotate-half pairing d <-> d + D/2 with full-length cos / sin tables, as in
+// examples/qwen_megakernel.py:90-107); q to q_out [M, Hq, D], k and v appended
+// at position `pos` of the caches [M, Hkv, S_cap, D].  One warp per (row, head),
+// lane d owns dims d and d + 32 (D = 64).
+__global__ void __launch_bounds__(32)
+qkv_finalize_kernel(const float* __restrict__ part, int splits, int M, int N, int Hq, int Hkv,
+                    const float* __restrict__ cosv, const float* __restrict__ sinv,
+                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kc,
+                    __nv_bfloat16* __restrict__ vc, int s_cap, int pos) {
+  constexpr int D = 64, H2 = 32;
+  const int m = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
+  const int c = head * D + d;
+  float lo = 0.f, hi = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float* p = part + (int64_t(s) * M + m) * N;
+    lo += p[c];
+    hi += p[c + H2];
+  }
+  if (head < Hq + Hkv) {
+    const float l2 = lo * cosv[d] - hi * sinv[d];
+    const float h2 = hi * cosv[d + H2] + lo * sinv[d + H2];
+    lo = l2;
+    hi = h2;
+  }
+  __nv_bfloat16* dst;
+  if (head < Hq) {
+    dst = q_out + (int64_t(m) * Hq + head) * D;
+  } else {
+    const int kvh = head < Hq + Hkv ? head - Hq : head - Hq - Hkv;
+    __nv_bfloat16* cache = head < Hq + Hkv ? kc : vc;
+    dst = cache + ((int64_t(m) * Hkv + kvh) * s_cap + pos) * D;
+  }
+  dst[d] = __float2bfloat16_rn(lo);
+  dst[d + H2] = __float2bfloat16_rn(hi);
+}
+
+// h = sum_s partial + residual (fp32), written as bf16 to h_out when given; then
+// y = rmsnorm(h) * w when y_out is given.  One CTA (256 threads) per row, N <= 2048.
+__global__ void __launch_bounds__(256)
+reduce_residual_norm_kernel(const float* __restrict__ part, int splits, int M, int N,
+                            const __nv_bfloat16* __restrict__ residual,
+                            __nv_bfloat16* __restrict__ h_out, const __nv_bfloat16* __restrict__ w,
+                            __nv_bfloat16* __restrict__ y_out, float eps) {
+  constexpr int kMaxPer = 8;
+  __shared__ float red[8];
+  const int m = blockIdx.x;
+  float h[kMaxPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int t = 0; t < kMaxPer; ++t) {
+    const int n = threadIdx.x + t * 256;
+    h[t] = 0.f;
+    if (n < N) {
+      float acc = residual ? bf(residual[int64_t(m) * N + n]) : 0.f;
+      for (int s = 0; s < splits; ++s) acc += part[(int64_t(s) * M + m) * N + n];
+      h[t] = acc;
+      ss = fmaf(acc, acc, ss);
+      if (h_out) h_out[int64_t(m) * N + n] = __float2bfloat16_rn(acc);
+    }
+  }
+  if (y_out == nullptr) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) total += red[i];
+  const float r = 1.0f / sqrtf(total / float(N) + eps);
+#pragma unroll
+  for (int t = 0; t < kMaxPer; ++t) {
+    const int n = threadIdx.x + t * 256;
+    if (n < N) y_out[int64_t(m) * N + n] = __float2bfloat16_rn(h[t] * r * bf(w[n]));
+  }
+}
+
+// act[m, j] = silu(g) * u with g = column j and u = column j + I of the summed
+// gate|up partials (N = 2 I); silu(g) = g / (1 + e^-g) (qwen_megakernel.py:212-216).
+__global__ void __launch_bounds__(256)
+swiglu_kernel(const float* __restrict__ part, int splits, int M, int I,
+              __nv_bfloat16* __restrict__ act) {
+  const int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x;
+  if (idx >= int64_t(M) * I) return;
+  const int m = int(idx / I), j = int(idx % I);
+  float g = 0.f, u = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float* p = part + (int64_t(s) * M + m) * (2 * I);
+    g += p[j];
+    u += p[j + I];
+  }
+  act[idx] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+}
+
+// ============================================================================ decode attention
+constexpr int DA_D = 64;
+constexpr int DA_GMAX = 8;         // query heads per kv head
+constexpr int DA_CHUNK = 1024;     // keys per CTA at most
+constexpr int DA_THREADS = 128;
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// One CTA per (sequence b, kv head, key chunk): scores of the G query heads of the
+// group against the chunk's keys (log2 domain), per-head max / sum, then
+// o[g, :] = sum_k p[g, k] V[k, :].  Writes unnormalised partials for the combine.
+//   q      [B, Hq, D] bf16 (RoPE applied), kc / vc [B, Hkv, cap, D] bf16, L keys valid
+//   opart  [B*Hkv, nsplit, G, D] fp32, mlpart [B*Hkv, nsplit, G, 2] fp32 (max, sum)
+__global__ void __launch_bounds__(DA_THREADS)
+decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
+                         const __nv_bfloat16* __restrict__ vc, float* __restrict__ opart,
+                         float* __restrict__ mlpart, int Hq, int Hkv, int cap, int L, int chunk,
+                         float scale_log2) {
+  __shared__ float sq[DA_GMAX][DA_D];
+  __shared__ float sp[DA_GMAX][DA_CHUNK];
+  __shared__ float sml[DA_GMAX][2];
+  const int G = Hq / Hkv;
+  const int bhk = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
+  const int b = bhk / Hkv, kvh = bhk % Hkv;
+  const int k0 = split * chunk;
+  const int n = max(0, min(chunk, L - k0));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  for (int i = tid; i < G * DA_D; i += DA_THREADS)
+    sq[i / DA_D][i % DA_D] = bf(q[(int64_t(b) * Hq + kvh * G + i / DA_D) * DA_D + i % DA_D]) *
+                             scale_log2;
+  __syncthreads();
+
+  const __nv_bfloat16* kbase = kc + (int64_t(bhk) * cap + k0) * DA_D;
+  const __nv_bfloat16* vbase = vc + (int64_t(bhk) * cap + k0) * DA_D;
+  // Phase 1: scores, one key per thread per step; each thread reads its key row (128 B).
+  for (int j = tid; j < n; j += DA_THREADS) {
+    float kf[DA_D];
+    const uint4* kr = reinterpret_cast<const uint4*>(kbase + int64_t(j) * DA_D);
+#pragma unroll
+    for (int v = 0; v < DA_D / 8; ++v) {
+      const uint4 w = __ldg(kr + v);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        kf[v * 8 + 2 * e] = __uint_as_float(ws[e] << 16);
+        kf[v * 8 + 2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
+      }
+    }
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int d = 0; d < DA_D; ++d) s = fmaf(sq[g][d], kf[d], s);
+      sp[g][j] = s;
+    }
+  }
+  __syncthreads();
+  // Phase 2: per-head max and sum; p replaces the score.
+  for (int g = warp; g < G; g += DA_THREADS / 32) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, sp[g][j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float p = ex2f(sp[g][j] - m);
+      sp[g][j] = p;
+      l += p;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) {
+      sml[g][0] = m;
+      sml[g][1] = l;
+    }
+  }
+  __syncthreads();
+  // Phase 3: o[g, d] for d = tid % 64, heads g = tid / 64 + 2 i.
+  const int d = tid & (DA_D - 1), g0 = tid / DA_D;
+  float acc[DA_GMAX / 2];
+#pragma unroll
+  for (int i = 0; i < DA_GMAX / 2; ++i) acc[i] = 0.f;
+  for (int j = 0; j < n; ++j) {
+    const float v = bf(vbase[int64_t(j) * DA_D + d]);
+#pragma unroll
+    for (int i = 0; i < DA_GMAX / 2; ++i) {
+      const int g = g0 + 2 * i;
+      if (g < G) acc[i] = fmaf(sp[g][j], v, acc[i]);
+    }
+  }
+  const int64_t base = (int64_t(bhk) * nsplit + split) * G;
+#pragma unroll
+  for (int i = 0; i < DA_GMAX / 2; ++i) {
+    const int g = g0 + 2 * i;
+    if (g < G) opart[(base + g) * DA_D + d] = acc[i];
+  }
+  if (tid < G) {
+    mlpart[(base + tid) * 2] = sml[tid][0];
+    mlpart[(base + tid) * 2 + 1] = sml[tid][1];
+  }
+}
+
+// out[b, h*D + d] = sum_s 2^(m_s - M) o_s[d] / sum_s 2^(m_s - M) l_s  (bf16).
+__global__ void __launch_bounds__(DA_D)
+decode_attn_combine_kernel(const float* __restrict__ opart, const float* __restrict__ mlpart,
+                           __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int nsplit) {
+  const int G = Hq / Hkv;
+  const int bh = blockIdx.x;            // b * Hq + h
+  const int b = bh / Hq, h = bh % Hq;
+  const int bhk = b * Hkv + h / G, g = h % G;
+  const int d = threadIdx.x;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, mlpart[((int64_t(bhk) * nsplit + s) * G + g) * 2]);
+  float num = 0.f, den = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const int64_t i = (int64_t(bhk) * nsplit + s) * G + g;
+    const float m = mlpart[i * 2];
+    if (m == -INFINITY) continue;
+    const float w = ex2f(m - M);
+    num = fmaf(w, opart[i * DA_D + d], num);
+    den = fmaf(w, mlpart[i * 2 + 1], den);
+  }
+  out[int64_t(bh) * DA_D + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+}
+
+}  // namespace
+
+namespace enigma {
+
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                       uint64_t row_pitch_elems, uint32_t box_cols, uint32_t box_rows);
+
+namespace {
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Split-K factor: enough (tile, split) CTAs for ~2 per SM, at least 2 k-blocks per split.
+int pick_splits(int64_t N, int64_t K) {
+  const int64_t tiles = (N + SK_BN - 1) / SK_BN;
+  const int64_t kbs = (K + SK_BK - 1) / SK_BK;
+  int64_t s = (2 * int64_t(sm_count()) + tiles - 1) / tiles;
+  s = std::min<int64_t>(s, std::max<int64_t>(1, kbs / 2));
+  return int(std::max<int64_t>(1, s));
+}
+
+struct Layout {
+  size_t partial, xn, q, attn, h1, h1n, act, opart, mlpart, total;
+  int attn_splits, attn_chunk;
+};
+
+Layout plan(const enigma_decode_layer_desc& d) {
+  const int64_t B = d.batch, H = d.hidden, D = d.head_dim, Hq = d.heads_q, Hkv = d.heads_kv;
+  const int64_t I = d.intermediate, Nqkv = (Hq + 2 * Hkv) * D;
+  const int64_t L = d.position + 1;
+  const int64_t gemms[4][2] = {{Nqkv, H}, {H, Hq * D}, {2 * I, H}, {H, I}};
+  int64_t part = 0;
+  for (auto& g : gemms) part = std::max(part, pick_splits(g[0], g[1]) * B * g[0]);
+  Layout l;
+  // split the keys so (sequence, kv head, chunk) CTAs cover ~4 per SM
+  int64_t splits = std::max<int64_t>(1, (4 * int64_t(sm_count()) + B * Hkv - 1) / (B * Hkv));
+  splits = std::max<int64_t>(splits, (L + DA_CHUNK - 1) / DA_CHUNK);
+  int64_t chunk = (L + splits - 1) / splits;
+  splits = (L + chunk - 1) / chunk;
+  l.attn_splits = int(splits);
+  l.attn_chunk = int(chunk);
+  const int64_t G = Hq / Hkv;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = align256(off + bytes); return o; };
+  l.partial = take(size_t(part) * 4);
+  l.xn = take(size_t(B * H) * 2);
+  l.q = take(size_t(B * Hq * D) * 2);
+  l.attn = take(size_t(B * Hq * D) * 2);
+  l.h1 = take(size_t(B * H) * 2);
+  l.h1n = take(size_t(B * H) * 2);
+  l.act = take(size_t(B * I) * 2);
+  l.opart = take(size_t(B * Hkv * splits * G * D) * 4);
+  l.mlpart = take(size_t(B * Hkv * splits * G * 2) * 4);
+  l.total = off;
+  return l;
+}
+
+cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M, int64_t N,
+                        int64_t K, int splits, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  if (!make_tmap_bf16_2d(&ta, A, M, K, K, SK_BK, SK_BM) ||
+      !make_tmap_bf16_2d(&tb, Bw, K, N, N, SK_BN, SK_BK))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(gemm_splitk_tc_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+  if (e != cudaSuccess) return e;
+  const int kbs = int((K + SK_BK - 1) / SK_BK);
+  const int per = (kbs + splits - 1) / splits;
+  dim3 grid(unsigned((N + SK_BN - 1) / SK_BN), unsigned(splits));
+  gemm_splitk_tc_kernel<<<grid, SK_THREADS, SK_SMEM, s>>>(ta, tb, partial, int(M), int(N), int(K),
+                                                          per, device_status());
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t decode_workspace_bytes(const enigma_decode_layer_desc& d) { return plan(d).total; }
+
+cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x, void* out,
+                                void* ws, cudaStream_t s) {
+  const Layout l = plan(d);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  float* part = reinterpret_cast<float*>(w + l.partial);
+  auto bfp = [&](size_t o) { return reinterpret_cast<__nv_bfloat16*>(w + o); };
+  const int B = int(d.batch), H = int(d.hidden), D = int(d.head_dim);
+  const int Hq = int(d.heads_q), Hkv = int(d.heads_kv), I = int(d.intermediate);
+  const int Nqkv = (Hq + 2 * Hkv) * D;
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  cudaError_t e;
+#define ENIGMA_TRY(expr)           \
+  do {                             \
+    e = (expr);                    \
+    if (e != cudaSuccess) return e; \
+  } while (0)
+  // 1. input RMSNorm
+  ENIGMA_TRY(rmsnorm_launch(ENIGMA_DTYPE_BF16, x, d.w_in_norm, bfp(l.xn), B, H, d.eps, s));
+  // 2-3. QKV projection, RoPE, KV-cache append at `position`
+  int sp = pick_splits(Nqkv, H);
+  ENIGMA_TRY(splitk_gemm(bfp(l.xn), d.w_qkv, part, B, Nqkv, H, sp, s));
+  qkv_finalize_kernel<<<dim3(B, Hq + 2 * Hkv), 32, 0, s>>>(
+      part, sp, B, Nqkv, Hq, Hkv, d.rope_cos, d.rope_sin, bfp(l.q),
+      static_cast<__nv_bfloat16*>(d.k_cache), static_cast<__nv_bfloat16*>(d.v_cache),
+      int(d.cache_capacity), int(d.position));
+  ENIGMA_TRY(cudaGetLastError());
+  // 4-5. attention over position + 1 keys, split-KV then combine
+  decode_attn_split_kernel<<<dim3(B * Hkv, l.attn_splits), DA_THREADS, 0, s>>>(
+      bfp(l.q), static_cast<const __nv_bfloat16*>(d.k_cache),
+      static_cast<const __nv_bfloat16*>(d.v_cache), reinterpret_cast<float*>(w + l.opart),
+      reinterpret_cast<float*>(w + l.mlpart), Hq, Hkv, int(d.cache_capacity),
+      int(d.position + 1), l.attn_chunk, d.attn_scale * 1.4426950408889634f);
+  ENIGMA_TRY(cudaGetLastError());
+  decode_attn_combine_kernel<<<B * Hq, DA_D, 0, s>>>(reinterpret_cast<float*>(w + l.opart),
+                                                      reinterpret_cast<float*>(w + l.mlpart),
+                                                      bfp(l.attn), Hq, Hkv, l.attn_splits);
+  ENIGMA_TRY(cudaGetLastError());
+  // 6-7. O projection + residual(x) -> h1, post-attention RMSNorm -> h1n
+  sp = pick_splits(H, Hq * D);
+  ENIGMA_TRY(splitk_gemm(bfp(l.attn), d.w_o, part, B, H, Hq * D, sp, s));
+  reduce_residual_norm_kernel<<<B, 256, 0, s>>>(part, sp, B, H, xb, bfp(l.h1),
+                                                static_cast<const __nv_bfloat16*>(d.w_post_norm),
+                                                bfp(l.h1n), d.eps);
+  ENIGMA_TRY(cudaGetLastError());
+  // 8-9. gate|up projection, SwiGLU
+  sp = pick_splits(2 * I, H);
+  ENIGMA_TRY(splitk_gemm(bfp(l.h1n), d.w_gate_up, part, B, 2 * I, H, sp, s));
+  swiglu_kernel<<<unsigned((int64_t(B) * I + 255) / 256), 256, 0, s>>>(part, sp, B, I, bfp(l.act));
+  ENIGMA_TRY(cudaGetLastError());
+  // 10-11. down projection + residual(h1) -> out
+  sp = pick_splits(H, I);
+  ENIGMA_TRY(splitk_gemm(bfp(l.act), d.w_down, part, B, H, I, sp, s));
+  reduce_residual_norm_kernel<<<B, 256, 0, s>>>(part, sp, B, H, bfp(l.h1),
+                                                static_cast<__nv_bfloat16*>(out), nullptr,
+                                                nullptr, 0.f);
+  ENIGMA_TRY(cudaGetLastError());
+#undef ENIGMA_TRY
+  return cudaSuccess;
+}
+
+}  // namespace enigma

@@ -121,6 +121,49 @@ int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const v
                        "sdpa_strided");
 }
 
+namespace {
+int32_t check_decode(const enigma_decode_layer_desc* d) {
+  if (d == nullptr) return bad("decode: desc is NULL");
+  if (d->batch <= 0 || d->batch > 128) return bad("decode: batch must be in [1, 128]");
+  if (d->head_dim != 64) return bad("decode: head_dim must be 64");
+  if (d->heads_kv <= 0 || d->heads_q % d->heads_kv != 0 || d->heads_q / d->heads_kv > 8)
+    return bad("decode: heads_q must be a multiple of heads_kv, at most 8 per kv head");
+  if (d->hidden <= 0 || d->hidden > 2048 || d->hidden % 64 != 0)
+    return bad("decode: hidden must be a multiple of 64, at most 2048");
+  if (d->intermediate <= 0 || d->intermediate % 32 != 0)
+    return bad("decode: intermediate must be a positive multiple of 32");
+  if (((d->heads_q + 2 * d->heads_kv) * 64) % 64 != 0) return bad("decode: qkv width");
+  if (d->position < 0 || d->position >= d->cache_capacity)
+    return bad("decode: position must be in [0, cache_capacity)");
+  const void* ptrs[] = {d->w_in_norm, d->w_qkv, d->w_o, d->w_post_norm, d->w_gate_up,
+                        d->w_down, d->rope_cos, d->rope_sin, d->k_cache, d->v_cache};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned(p, 16)) return bad("decode: NULL or non-16-byte-aligned pointer");
+  return ENIGMA_OK;
+}
+}  // namespace
+
+int32_t enigma_decode_workspace_bytes(const enigma_decode_layer_desc* desc, size_t* bytes) {
+  int32_t rc = check_decode(desc);
+  if (rc != ENIGMA_OK) return rc;
+  if (bytes == nullptr) return bad("decode: bytes is NULL");
+  *bytes = enigma::decode_workspace_bytes(*desc);
+  return ENIGMA_OK;
+}
+
+int32_t enigma_decode_layer_bf16(const enigma_decode_layer_desc* desc, const void* x, void* out,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  int32_t rc = check_decode(desc);
+  if (rc != ENIGMA_OK) return rc;
+  if (x == nullptr || out == nullptr || workspace == nullptr || !aligned(x, 16) ||
+      !aligned(out, 16) || !aligned(workspace, 256))
+    return bad("decode: x / out must be 16-byte aligned, workspace 256-byte aligned");
+  if (workspace_bytes < enigma::decode_workspace_bytes(*desc))
+    return bad("decode: workspace smaller than enigma_decode_workspace_bytes()");
+  return launch_status(enigma::decode_layer_launch(*desc, x, out, workspace, as_stream(stream)),
+                       "decode_layer");
+}
+
 int32_t enigma_dispatch(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
                         const int64_t* ip, int32_t n_ip, const float* fp, int32_t n_fp,
                         const uint32_t* grid3, const uint32_t* threads3, void* stream) {

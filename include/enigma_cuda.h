@@ -119,6 +119,28 @@ int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const v
                             int64_t seq_kv, int64_t head_dim, const int64_t* strides12,
                             float scale, int32_t causal, void* stream);
 
+/* ---- one decoder-layer decode step (Qwen-style; the reference's qwen_fused megakernel,
+ *      examples/qwen_megakernel.py:228-269, at BASELINE config 5 shapes) ----
+ * x, out: [batch, hidden] bf16.  Weights bf16, row-major [in, out]:
+ *   w_qkv [hidden, (heads_q + 2 heads_kv) * head_dim]   (q heads | k heads | v heads)
+ *   w_o [heads_q * head_dim, hidden], w_gate_up [hidden, 2 * intermediate] (gate | up),
+ *   w_down [intermediate, hidden]; w_in_norm / w_post_norm [hidden].
+ * rope_cos / rope_sin: fp32 [head_dim] rotate-half tables for `position`.
+ * k_cache / v_cache: bf16 [batch, heads_kv, cache_capacity, head_dim]; the step writes
+ * the new token's k, v at `position` and attends over position + 1 keys.
+ * head_dim must be 64; heads_q / heads_kv <= 8; hidden <= 2048; batch <= 128.
+ * workspace: caller-owned device memory of enigma_decode_workspace_bytes() bytes. */
+typedef struct enigma_decode_layer_desc {
+  int64_t batch, hidden, heads_q, heads_kv, head_dim, intermediate, cache_capacity, position;
+  float eps, attn_scale;
+  const void *w_in_norm, *w_qkv, *w_o, *w_post_norm, *w_gate_up, *w_down;
+  const float *rope_cos, *rope_sin;
+  void *k_cache, *v_cache;
+} enigma_decode_layer_desc;
+int32_t enigma_decode_workspace_bytes(const enigma_decode_layer_desc* desc, size_t* bytes);
+int32_t enigma_decode_layer_bf16(const enigma_decode_layer_desc* desc, const void* x, void* out,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- generic dispatch by kernel id: replaces enigma_dispatch /
  *      enigma_dispatch_timed (libenigma_runtime.swift:132-214).
  *      grid / threads are Metal-style totals (threads per axis, not groups),

@@ -123,3 +123,49 @@ def rel_fro(a, b) -> float:
     b = np.asarray(b, np.float64)
     den = np.linalg.norm(b)
     return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))
+
+
+# --------------------------------------------------------------------------- decode layer
+def decode_layer(x, w, k_cache, v_cache, cos, sin, position, heads_q, heads_kv, head_dim,
+                 eps):
+    """One decode step, restating full_decode_np (examples/qwen_megakernel.py:320-342)
+    for a batch, bf16 weights given as fp32 arrays, no q/k head-norm.
+
+    x [B, H]; k_cache / v_cache [B, Hkv, cap, D] with `position` valid entries (the new
+    k, v are placed at `position`, the caches are not modified); cos / sin [D].
+    Returns (out [B, H], q_rot, k_new, v_new).  fp64 internally.
+    """
+    x = np.asarray(x, np.float64)
+    f = {k: np.asarray(v, np.float64) for k, v in w.items()}
+    B, H = x.shape
+    D, G = head_dim, heads_q // heads_kv
+    half = D // 2
+
+    def rms(v, wt):
+        return v / np.sqrt(np.mean(v * v, axis=-1, keepdims=True) + eps) * wt
+
+    def rope(t):  # t [..., D]
+        lo, hi = t[..., :half], t[..., half:]
+        return np.concatenate([lo * cos[:half] - hi * sin[:half],
+                               hi * cos[half:] + lo * sin[half:]], axis=-1)
+
+    xn = rms(x, f["w_in_norm"])
+    qkv = xn @ f["w_qkv"]
+    q = rope(qkv[:, :heads_q * D].reshape(B, heads_q, D))
+    k = rope(qkv[:, heads_q * D:(heads_q + heads_kv) * D].reshape(B, heads_kv, D))
+    v = qkv[:, (heads_q + heads_kv) * D:].reshape(B, heads_kv, D)
+    kc = np.asarray(k_cache[:, :, :position], np.float64)
+    vc = np.asarray(v_cache[:, :, :position], np.float64)
+    K = np.concatenate([kc, k[:, :, None]], axis=2)          # [B, Hkv, L, D]
+    V = np.concatenate([vc, v[:, :, None]], axis=2)
+    attn = np.empty((B, heads_q, D))
+    for h in range(heads_q):
+        s = np.einsum("bd,bld->bl", q[:, h], K[:, h // G]) / np.sqrt(D)
+        p = np.exp(s - s.max(axis=1, keepdims=True))
+        attn[:, h] = np.einsum("bl,bld->bd", p / p.sum(axis=1, keepdims=True), V[:, h // G])
+    h1 = x + attn.reshape(B, heads_q * D) @ f["w_o"]
+    gu = rms(h1, f["w_post_norm"]) @ f["w_gate_up"]
+    inter = gu.shape[1] // 2
+    g, u = gu[:, :inter], gu[:, inter:]
+    out = h1 + (g / (1 + np.exp(-g)) * u) @ f["w_down"]
+    return out.astype(np.float32), q.astype(np.float32), k.astype(np.float32), v.astype(np.float32)
