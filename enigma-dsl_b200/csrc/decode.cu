@@ -407,13 +407,20 @@ Layout plan(const enigma_decode_layer_desc& d) {
   int64_t part = 0;
   for (auto& g : gemms) part = std::max(part, pick_splits(g[0], g[1]) * B * g[0]);
   Layout l;
-  // split the keys so (sequence, kv head, chunk) CTAs cover ~4 per SM
-  int64_t splits = std::max<int64_t>(1, (4 * int64_t(sm_count()) + B * Hkv - 1) / (B * Hkv));
-  splits = std::max<int64_t>(splits, (L + DA_CHUNK - 1) / DA_CHUNK);
-  int64_t chunk = (L + splits - 1) / splits;
-  splits = (L + chunk - 1) / chunk;
-  l.attn_splits = int(splits);
+  // Split the keys so (sequence, kv head, chunk) CTAs cover ~4 per SM; chunks hold at most
+  // DA_CHUNK keys.  The workspace is sized for the largest split count any position up to
+  // the cache capacity can need, so one workspace serves every step.
+  const int64_t target = std::max<int64_t>(1, (4 * int64_t(sm_count()) + B * Hkv - 1) / (B * Hkv));
+  auto split_for = [&](int64_t keys, int64_t* chunk_out) {
+    int64_t sp = std::max<int64_t>(target, (keys + DA_CHUNK - 1) / DA_CHUNK);
+    int64_t ch = (keys + sp - 1) / sp;
+    if (chunk_out) *chunk_out = ch;
+    return (keys + ch - 1) / ch;
+  };
+  int64_t chunk = 0;
+  l.attn_splits = int(split_for(L, &chunk));
   l.attn_chunk = int(chunk);
+  const int64_t splits = std::max<int64_t>(target, (d.cache_capacity + DA_CHUNK - 1) / DA_CHUNK);
   const int64_t G = Hq / Hkv;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align256(off + bytes); return o; };
