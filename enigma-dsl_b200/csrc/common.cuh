@@ -18,6 +18,9 @@ uint32_t* device_status();
 // Operator launchers (asynchronous).  Arguments are validated by the C ABI layer.
 cudaError_t rmsnorm_launch(int dtype, const void* x, const void* w, void* y, int64_t rows,
                            int64_t hidden, float eps, cudaStream_t s);
+// Same, with the SM count given (no per-device state is touched).
+cudaError_t rmsnorm_launch_sms(int dtype, const void* x, const void* w, void* y, int64_t rows,
+                               int64_t hidden, float eps, int sms, cudaStream_t s);
 cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
                              int64_t K, cudaStream_t s);
 cudaError_t gemm_f32_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
@@ -36,6 +39,9 @@ cudaError_t sdpa_bf16_launch(const void* Q, const void* K, const void* V, void* 
 size_t decode_workspace_bytes(const enigma_decode_layer_desc& d);
 cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x, void* out,
                                 void* ws, cudaStream_t s);
+
+// Argument checks of a decode-layer descriptor (ENIGMA_OK or ENIGMA_ERR_BADARG + message).
+int32_t check_decode_desc(const enigma_decode_layer_desc* d);
 
 // Records a message for enigma_last_error on the calling thread.
 void set_error(const char* fmt, ...);

@@ -386,10 +386,10 @@ namespace {
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // Split-K factor: enough (tile, split) CTAs for ~2 per SM, at least 2 k-blocks per split.
-int pick_splits(int64_t N, int64_t K) {
+int pick_splits(int64_t N, int64_t K, int sms) {
   const int64_t tiles = (N + SK_BN - 1) / SK_BN;
   const int64_t kbs = (K + SK_BK - 1) / SK_BK;
-  int64_t s = (2 * int64_t(sm_count()) + tiles - 1) / tiles;
+  int64_t s = (2 * int64_t(sms) + tiles - 1) / tiles;
   s = std::min<int64_t>(s, std::max<int64_t>(1, kbs / 2));
   return int(std::max<int64_t>(1, s));
 }
@@ -399,18 +399,18 @@ struct Layout {
   int attn_splits, attn_chunk;
 };
 
-Layout plan(const enigma_decode_layer_desc& d) {
+Layout plan(const enigma_decode_layer_desc& d, int sms) {
   const int64_t B = d.batch, H = d.hidden, D = d.head_dim, Hq = d.heads_q, Hkv = d.heads_kv;
   const int64_t I = d.intermediate, Nqkv = (Hq + 2 * Hkv) * D;
   const int64_t L = d.position + 1;
   const int64_t gemms[4][2] = {{Nqkv, H}, {H, Hq * D}, {2 * I, H}, {H, I}};
   int64_t part = 0;
-  for (auto& g : gemms) part = std::max(part, pick_splits(g[0], g[1]) * B * g[0]);
+  for (auto& g : gemms) part = std::max(part, pick_splits(g[0], g[1], sms) * B * g[0]);
   Layout l;
   // Split the keys so (sequence, kv head, chunk) CTAs cover ~4 per SM; chunks hold at most
   // DA_CHUNK keys.  The workspace is sized for the largest split count any position up to
   // the cache capacity can need, so one workspace serves every step.
-  const int64_t target = std::max<int64_t>(1, (4 * int64_t(sm_count()) + B * Hkv - 1) / (B * Hkv));
+  const int64_t target = std::max<int64_t>(1, (4 * int64_t(sms) + B * Hkv - 1) / (B * Hkv));
   auto split_for = [&](int64_t keys, int64_t* chunk_out) {
     int64_t sp = std::max<int64_t>(target, (keys + DA_CHUNK - 1) / DA_CHUNK);
     int64_t ch = (keys + sp - 1) / sp;
@@ -438,7 +438,7 @@ Layout plan(const enigma_decode_layer_desc& d) {
 }
 
 cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M, int64_t N,
-                        int64_t K, int splits, cudaStream_t s) {
+                        int64_t K, int splits, uint32_t* status, cudaStream_t s) {
   CUtensorMap ta, tb;
   if (!make_tmap_bf16_2d(&ta, A, M, K, K, SK_BK, SK_BM) ||
       !make_tmap_bf16_2d(&tb, Bw, K, N, N, SK_BN, SK_BK))
@@ -450,17 +450,16 @@ cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M
   const int per = (kbs + splits - 1) / splits;
   dim3 grid(unsigned((N + SK_BN - 1) / SK_BN), unsigned(splits));
   gemm_splitk_tc_kernel<<<grid, SK_THREADS, SK_SMEM, s>>>(ta, tb, partial, int(M), int(N), int(K),
-                                                          per, device_status());
+                                                          per, status);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-size_t decode_workspace_bytes(const enigma_decode_layer_desc& d) { return plan(d).total; }
-
-cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x, void* out,
-                                void* ws, cudaStream_t s) {
-  const Layout l = plan(d);
+// The whole step with an explicit SM count and status word (no per-device state used).
+cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, void* out,
+                             void* ws, int sms, uint32_t* status, cudaStream_t s) {
+  const Layout l = plan(d, sms);
   uint8_t* w = static_cast<uint8_t*>(ws);
   float* part = reinterpret_cast<float*>(w + l.partial);
   auto bfp = [&](size_t o) { return reinterpret_cast<__nv_bfloat16*>(w + o); };
@@ -475,10 +474,10 @@ cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x
     if (e != cudaSuccess) return e; \
   } while (0)
   // 1. input RMSNorm
-  ENIGMA_TRY(rmsnorm_launch(ENIGMA_DTYPE_BF16, x, d.w_in_norm, bfp(l.xn), B, H, d.eps, s));
+  ENIGMA_TRY(rmsnorm_launch_sms(ENIGMA_DTYPE_BF16, x, d.w_in_norm, bfp(l.xn), B, H, d.eps, sms, s));
   // 2-3. QKV projection, RoPE, KV-cache append at `position`
-  int sp = pick_splits(Nqkv, H);
-  ENIGMA_TRY(splitk_gemm(bfp(l.xn), d.w_qkv, part, B, Nqkv, H, sp, s));
+  int sp = pick_splits(Nqkv, H, sms);
+  ENIGMA_TRY(splitk_gemm(bfp(l.xn), d.w_qkv, part, B, Nqkv, H, sp, status, s));
   qkv_finalize_kernel<<<dim3(B, Hq + 2 * Hkv), 32, 0, s>>>(
       part, sp, B, Nqkv, Hq, Hkv, d.rope_cos, d.rope_sin, bfp(l.q),
       static_cast<__nv_bfloat16*>(d.k_cache), static_cast<__nv_bfloat16*>(d.v_cache),
@@ -496,20 +495,20 @@ cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x
                                                       bfp(l.attn), Hq, Hkv, l.attn_splits);
   ENIGMA_TRY(cudaGetLastError());
   // 6-7. O projection + residual(x) -> h1, post-attention RMSNorm -> h1n
-  sp = pick_splits(H, Hq * D);
-  ENIGMA_TRY(splitk_gemm(bfp(l.attn), d.w_o, part, B, H, Hq * D, sp, s));
+  sp = pick_splits(H, Hq * D, sms);
+  ENIGMA_TRY(splitk_gemm(bfp(l.attn), d.w_o, part, B, H, Hq * D, sp, status, s));
   reduce_residual_norm_kernel<<<B, 256, 0, s>>>(part, sp, B, H, xb, bfp(l.h1),
                                                 static_cast<const __nv_bfloat16*>(d.w_post_norm),
                                                 bfp(l.h1n), d.eps);
   ENIGMA_TRY(cudaGetLastError());
   // 8-9. gate|up projection, SwiGLU
-  sp = pick_splits(2 * I, H);
-  ENIGMA_TRY(splitk_gemm(bfp(l.h1n), d.w_gate_up, part, B, 2 * I, H, sp, s));
+  sp = pick_splits(2 * I, H, sms);
+  ENIGMA_TRY(splitk_gemm(bfp(l.h1n), d.w_gate_up, part, B, 2 * I, H, sp, status, s));
   swiglu_kernel<<<unsigned((int64_t(B) * I + 255) / 256), 256, 0, s>>>(part, sp, B, I, bfp(l.act));
   ENIGMA_TRY(cudaGetLastError());
   // 10-11. down projection + residual(h1) -> out
-  sp = pick_splits(H, I);
-  ENIGMA_TRY(splitk_gemm(bfp(l.act), d.w_down, part, B, H, I, sp, s));
+  sp = pick_splits(H, I, sms);
+  ENIGMA_TRY(splitk_gemm(bfp(l.act), d.w_down, part, B, H, I, sp, status, s));
   reduce_residual_norm_kernel<<<B, 256, 0, s>>>(part, sp, B, H, bfp(l.h1),
                                                 static_cast<__nv_bfloat16*>(out), nullptr,
                                                 nullptr, 0.f);
@@ -518,4 +517,14 @@ cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x
   return cudaSuccess;
 }
 
+size_t decode_workspace_bytes(const enigma_decode_layer_desc& d) {
+  return plan(d, sm_count()).total;
+}
+
+cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x, void* out,
+                                void* ws, cudaStream_t s) {
+  return decode_layer_run(d, x, out, ws, sm_count(), device_status(), s);
+}
+
 }  // namespace enigma
+

@@ -121,8 +121,10 @@ int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const v
                        "sdpa_strided");
 }
 
-namespace {
-int32_t check_decode(const enigma_decode_layer_desc* d) {
+}  // extern "C"
+
+namespace enigma {
+int32_t check_decode_desc(const enigma_decode_layer_desc* d) {
   if (d == nullptr) return bad("decode: desc is NULL");
   if (d->batch <= 0 || d->batch > 128) return bad("decode: batch must be in [1, 128]");
   if (d->head_dim != 64) return bad("decode: head_dim must be 64");
@@ -141,10 +143,12 @@ int32_t check_decode(const enigma_decode_layer_desc* d) {
     if (p == nullptr || !aligned(p, 16)) return bad("decode: NULL or non-16-byte-aligned pointer");
   return ENIGMA_OK;
 }
-}  // namespace
+}  // namespace enigma
+
+extern "C" {
 
 int32_t enigma_decode_workspace_bytes(const enigma_decode_layer_desc* desc, size_t* bytes) {
-  int32_t rc = check_decode(desc);
+  int32_t rc = enigma::check_decode_desc(desc);
   if (rc != ENIGMA_OK) return rc;
   if (bytes == nullptr) return bad("decode: bytes is NULL");
   *bytes = enigma::decode_workspace_bytes(*desc);
@@ -153,7 +157,7 @@ int32_t enigma_decode_workspace_bytes(const enigma_decode_layer_desc* desc, size
 
 int32_t enigma_decode_layer_bf16(const enigma_decode_layer_desc* desc, const void* x, void* out,
                                  void* workspace, size_t workspace_bytes, void* stream) {
-  int32_t rc = check_decode(desc);
+  int32_t rc = enigma::check_decode_desc(desc);
   if (rc != ENIGMA_OK) return rc;
   if (x == nullptr || out == nullptr || workspace == nullptr || !aligned(x, 16) ||
       !aligned(out, 16) || !aligned(workspace, 256))

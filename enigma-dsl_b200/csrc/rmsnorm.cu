@@ -157,9 +157,9 @@ rmsnorm_generic_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __re
 
 template <typename T, int THREADS, int NV>
 cudaError_t launch_row(const void* x, const void* w, void* y, int64_t rows, int64_t hidden,
-                       float eps, cudaStream_t s) {
+                       float eps, int sms, cudaStream_t s) {
   // Enough CTAs to fill every SM several times over; each CTA strides over rows.
-  const int64_t max_ctas = int64_t(enigma::sm_count()) * (2048 / THREADS) * 8;
+  const int64_t max_ctas = int64_t(sms) * (2048 / THREADS) * 8;
   const int grid = int(rows < max_ctas ? rows : max_ctas);
   rmsnorm_row_kernel<T, THREADS, NV><<<grid, THREADS, 0, s>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), static_cast<T*>(y), rows,
@@ -169,7 +169,7 @@ cudaError_t launch_row(const void* x, const void* w, void* y, int64_t rows, int6
 
 template <typename T>
 cudaError_t dispatch(const void* x, const void* w, void* y, int64_t rows, int64_t hidden,
-                     float eps, cudaStream_t s) {
+                     float eps, int sms, cudaStream_t s) {
   constexpr int VE = Vec<T>::kElems;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
@@ -178,17 +178,17 @@ cudaError_t dispatch(const void* x, const void* w, void* y, int64_t rows, int64_
     const int64_t vecs = hidden / VE;  // 16-byte vectors per row
     // Pick (threads, vectors/thread) with threads <= 256 and at most 8 vectors held.
     switch (vecs) {
-      case 32:   return launch_row<T, 32, 1>(x, w, y, rows, hidden, eps, s);
-      case 64:   return launch_row<T, 64, 1>(x, w, y, rows, hidden, eps, s);
-      case 128:  return launch_row<T, 128, 1>(x, w, y, rows, hidden, eps, s);
-      case 256:  return launch_row<T, 128, 2>(x, w, y, rows, hidden, eps, s);
-      case 512:  return launch_row<T, 128, 4>(x, w, y, rows, hidden, eps, s);
-      case 1024: return launch_row<T, 256, 4>(x, w, y, rows, hidden, eps, s);
-      case 2048: return launch_row<T, 256, 8>(x, w, y, rows, hidden, eps, s);
+      case 32:   return launch_row<T, 32, 1>(x, w, y, rows, hidden, eps, sms, s);
+      case 64:   return launch_row<T, 64, 1>(x, w, y, rows, hidden, eps, sms, s);
+      case 128:  return launch_row<T, 128, 1>(x, w, y, rows, hidden, eps, sms, s);
+      case 256:  return launch_row<T, 128, 2>(x, w, y, rows, hidden, eps, sms, s);
+      case 512:  return launch_row<T, 128, 4>(x, w, y, rows, hidden, eps, sms, s);
+      case 1024: return launch_row<T, 256, 4>(x, w, y, rows, hidden, eps, sms, s);
+      case 2048: return launch_row<T, 256, 8>(x, w, y, rows, hidden, eps, sms, s);
       default: break;
     }
   }
-  const int64_t max_ctas = int64_t(enigma::sm_count()) * 16;
+  const int64_t max_ctas = int64_t(sms) * 16;
   const int grid = int(rows < max_ctas ? rows : max_ctas);
   rmsnorm_generic_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x),
                                                  static_cast<const T*>(w), static_cast<T*>(y),
@@ -199,10 +199,15 @@ cudaError_t dispatch(const void* x, const void* w, void* y, int64_t rows, int64_
 }  // namespace
 
 namespace enigma {
+cudaError_t rmsnorm_launch_sms(int dtype, const void* x, const void* w, void* y, int64_t rows,
+                               int64_t hidden, float eps, int sms, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  if (dtype == ENIGMA_DTYPE_F32) return dispatch<float>(x, w, y, rows, hidden, eps, sms, s);
+  return dispatch<__nv_bfloat16>(x, w, y, rows, hidden, eps, sms, s);
+}
+
 cudaError_t rmsnorm_launch(int dtype, const void* x, const void* w, void* y, int64_t rows,
                            int64_t hidden, float eps, cudaStream_t s) {
-  if (rows == 0) return cudaSuccess;
-  if (dtype == ENIGMA_DTYPE_F32) return dispatch<float>(x, w, y, rows, hidden, eps, s);
-  return dispatch<__nv_bfloat16>(x, w, y, rows, hidden, eps, s);
+  return rmsnorm_launch_sms(dtype, x, w, y, rows, hidden, eps, sm_count(), s);
 }
 }  // namespace enigma
