@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -528,3 +529,105 @@ cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x
 
 }  // namespace enigma
 
+// ============================================================================ no-allocation entry
+// Some callers cannot call cudaMalloc on the path that runs a decode step: a real-time
+// serving loop that must not enter the allocator (which can synchronize or stall), a
+// plugin inside another runtime that owns all device memory, or code running where an
+// allocation failure is not allowed to happen mid-step.  enigma_decode_layer_bf16_noalloc
+// serves them: it runs the same kernels as enigma_decode_layer_bf16, with the workspace
+// in a fixed device array compiled into this library instead of caller memory.
+//
+// The array costs kNoAllocScratchBytes on every GPU that loads the library, until the
+// process exits.  All calls share it and it keeps the previous call's contents: every
+// byte a step reads from it is written earlier in the same step, so nothing needs
+// clearing except the status word, which is zeroed at the start of each call.  Calls
+// that overlap on the GPU (different streams, or different host threads on one device)
+// race on the array; serialize them on one stream.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) uint32_t g_noalloc_status[64];
+
+struct NoAllocDevice {
+  bool ready = false;
+  uint8_t* scratch = nullptr;   // device address of g_noalloc_scratch on this device
+  uint32_t* status = nullptr;   // device address of g_noalloc_status on this device
+  int sms = 0;
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: resolve the arrays' device addresses.  In
+// host code the array names are host-side stand-ins, not device addresses; only the
+// addresses returned by cudaGetSymbolAddress may be given to a kernel.
+int32_t noalloc_setup(NoAllocDevice** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    enigma::set_error("decode noalloc: no current CUDA device (%s)", cudaGetErrorString(e));
+    return ENIGMA_ERR_DEVICE;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      enigma::set_error("decode noalloc: cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+      return ENIGMA_ERR_DEVICE;
+    }
+    void* st = nullptr;
+    e = cudaGetSymbolAddress(&st, g_noalloc_status);
+    if (e != cudaSuccess) {
+      enigma::set_error("decode noalloc: cudaGetSymbolAddress(status) failed: %s", cudaGetErrorString(e));
+      return ENIGMA_ERR_DEVICE;
+    }
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess || sms <= 0) {
+      enigma::set_error("decode noalloc: SM count query failed: %s", cudaGetErrorString(e));
+      return ENIGMA_ERR_DEVICE;
+    }
+    d.scratch = static_cast<uint8_t*>(p);
+    d.status = static_cast<uint32_t*>(st);
+    d.sms = sms;
+    d.ready = true;
+  }
+  *out = &d;
+  return ENIGMA_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t enigma_decode_layer_bf16_noalloc(const enigma_decode_layer_desc* desc,
+                                                    const void* x, void* out, void* stream) {
+  int32_t rc = enigma::check_decode_desc(desc);
+  if (rc != ENIGMA_OK) return rc;
+  if (x == nullptr || out == nullptr || reinterpret_cast<uintptr_t>(x) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(out) % 16 != 0) {
+    enigma::set_error("bad argument: decode noalloc: x / out must be non-NULL and 16-byte aligned");
+    return ENIGMA_ERR_BADARG;
+  }
+  NoAllocDevice* dev = nullptr;
+  rc = noalloc_setup(&dev);
+  if (rc != ENIGMA_OK) return rc;
+  const size_t need = enigma::plan(*desc, dev->sms).total;
+  if (need > kNoAllocScratchBytes) {
+    enigma::set_error("bad argument: decode noalloc: this step needs %zu bytes of scratch, more than "
+              "the fixed %zu-byte array of the no-allocation entry point; use "
+              "enigma_decode_layer_bf16 with a caller-provided workspace",
+              need, kNoAllocScratchBytes);
+    return ENIGMA_ERR_BADARG;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(dev->status, 0, sizeof(uint32_t), s);
+  if (e == cudaSuccess)
+    e = enigma::decode_layer_run(*desc, x, out, dev->scratch, dev->sms, dev->status, s);
+  if (e != cudaSuccess) {
+    enigma::set_error("decode noalloc launch failed: %s (%s)", cudaGetErrorName(e), cudaGetErrorString(e));
+    return ENIGMA_ERR_LAUNCH;
+  }
+  return ENIGMA_OK;
+}

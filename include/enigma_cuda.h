@@ -141,6 +141,20 @@ int32_t enigma_decode_workspace_bytes(const enigma_decode_layer_desc* desc, size
 int32_t enigma_decode_layer_bf16(const enigma_decode_layer_desc* desc, const void* x, void* out,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same decode step without a caller-provided workspace, for callers that cannot
+ * allocate device memory on this path: a serving loop that must never enter the
+ * allocator, a plugin inside a host runtime that owns all device memory, code where an
+ * allocation failure mid-step is not acceptable.  (No counterpart in the reference: its
+ * Metal runtime always allocates buffers per call.)  The workspace is a fixed 16 MiB
+ * device array inside this library, held on every GPU that loads it until the process
+ * exits; a step that needs more (enigma_decode_workspace_bytes) is rejected with
+ * ENIGMA_ERR_BADARG.  This call itself allocates nothing.  Its first call on a device
+ * looks up the array's device address once (cudaGetSymbolAddress), so make that first
+ * call before any stream capture.  All calls share the array: calls that overlap on the
+ * GPU race, so serialize them on one stream. */
+int32_t enigma_decode_layer_bf16_noalloc(const enigma_decode_layer_desc* desc, const void* x,
+                                         void* out, void* stream);
+
 /* ---- generic dispatch by kernel id: replaces enigma_dispatch /
  *      enigma_dispatch_timed (libenigma_runtime.swift:132-214).
  *      grid / threads are Metal-style totals (threads per axis, not groups),
