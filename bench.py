@@ -376,6 +376,20 @@ def run_single_op(args):
     stream = torch.cuda.current_stream()
     g = torch.Generator(device="cuda").manual_seed(0)
     n = args.size
+    if args.only == "decode":
+        from enigma.decode_layer import DecodeConfig, DecodeLayer
+        layer = DecodeLayer.random(DecodeConfig(), seed=0)
+        x = torch.randn(64, 896, device="cuda", generator=g).bfloat16()
+        out = torch.empty_like(x)
+        fn = lambda: layer.step(x, out=out)  # noqa: E731
+        for _ in range(args.warmup):
+            fn()
+        ms = _time_device(fn, args.steps, stream)
+        cuda_ops.synchronize(0)
+        print(json.dumps({"op": "decode", "ms": round(ms, 4),
+                          "gbs": round((layer.weight_bytes() + 2 * 64 * 2 * 2049 * 64 * 2)
+                                       / (ms * 1e-3) / 1e9, 1)}), flush=True)
+        return
     if args.only == "gemm":
         a = (torch.randn(n, n, device="cuda", generator=g) / math.sqrt(n)).bfloat16()
         b = torch.randn(n, n, device="cuda", generator=g).bfloat16()
@@ -408,7 +422,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=16384)
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (smaller cases are for profiling only)")
-    ap.add_argument("--only", choices=["gemm", "sdpa", "sdpa_causal"], default=None,
+    ap.add_argument("--only", choices=["gemm", "sdpa", "sdpa_causal", "decode"], default=None,
                     help="time one operator alone (profiling case)")
     ap.add_argument("--size", type=int, default=4096, help="--only: n for GEMM n^3, S for SDPA")
     args = ap.parse_args()
