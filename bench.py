@@ -237,7 +237,7 @@ def _decode_side(hbm_peak):
     x = torch.randn(cfg.batch, cfg.hidden, device="cuda").bfloat16()
     out = torch.empty_like(x)
     stream = torch.cuda.current_stream()
-    fn = lambda: layer.step(x, out=out)  # noqa: E731
+    fn = layer.capture(x, out)
     for _ in range(5):
         fn()
     ms = _time_device(fn, 50, stream)
@@ -381,7 +381,7 @@ def run_single_op(args):
         layer = DecodeLayer.random(DecodeConfig(), seed=0)
         x = torch.randn(64, 896, device="cuda", generator=g).bfloat16()
         out = torch.empty_like(x)
-        fn = lambda: layer.step(x, out=out)  # noqa: E731
+        fn = layer.capture(x, out) if args.graph else (lambda: layer.step(x, out=out))
         for _ in range(args.warmup):
             fn()
         ms = _time_device(fn, args.steps, stream)
@@ -424,6 +424,7 @@ def main():
                     help="rows per GPU (smaller cases are for profiling only)")
     ap.add_argument("--only", choices=["gemm", "sdpa", "sdpa_causal", "decode"], default=None,
                     help="time one operator alone (profiling case)")
+    ap.add_argument("--graph", action="store_true", help="--only decode: replay a CUDA graph")
     ap.add_argument("--size", type=int, default=4096, help="--only: n for GEMM n^3, S for SDPA")
     args = ap.parse_args()
     _set_rows(args.rows)

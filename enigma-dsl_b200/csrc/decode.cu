@@ -190,27 +190,39 @@ qkv_finalize_kernel(const float* __restrict__ part, int splits, int M, int N, in
 }
 
 // h = sum_s partial + residual (fp32), written as bf16 to h_out when given; then
-// y = rmsnorm(h) * w when y_out is given.  One CTA (256 threads) per row, N <= 2048.
+// y = rmsnorm(h) * w when y_out is given.  One CTA (256 threads) per row, each thread
+// four adjacent columns (float4 partial loads, all splits in flight); N % 4 == 0, N <= 2048.
 __global__ void __launch_bounds__(256)
 reduce_residual_norm_kernel(const float* __restrict__ part, int splits, int M, int N,
                             const __nv_bfloat16* __restrict__ residual,
                             __nv_bfloat16* __restrict__ h_out, const __nv_bfloat16* __restrict__ w,
                             __nv_bfloat16* __restrict__ y_out, float eps) {
-  constexpr int kMaxPer = 8;
+  constexpr int kPer = 2;  // float4 groups per thread: 256 * 2 * 4 = 2048 columns
   __shared__ float red[8];
   const int m = blockIdx.x;
-  float h[kMaxPer];
+  float4 h[kPer];
   float ss = 0.f;
 #pragma unroll
-  for (int t = 0; t < kMaxPer; ++t) {
-    const int n = threadIdx.x + t * 256;
-    h[t] = 0.f;
+  for (int t = 0; t < kPer; ++t) {
+    const int n = (threadIdx.x + t * 256) * 4;
+    h[t] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (n < N) {
-      float acc = residual ? bf(residual[int64_t(m) * N + n]) : 0.f;
-      for (int s = 0; s < splits; ++s) acc += part[(int64_t(s) * M + m) * N + n];
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (residual) {
+        const uint2 r = *reinterpret_cast<const uint2*>(residual + int64_t(m) * N + n);
+        acc = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                          __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+      }
+#pragma unroll 4
+      for (int s = 0; s < splits; ++s) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(part + (int64_t(s) * M + m) * N + n));
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
       h[t] = acc;
-      ss = fmaf(acc, acc, ss);
-      if (h_out) h_out[int64_t(m) * N + n] = __float2bfloat16_rn(acc);
+      ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+      if (h_out)
+        *reinterpret_cast<uint2*>(h_out + int64_t(m) * N + n) =
+            make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
     }
   }
   if (y_out == nullptr) return;
@@ -223,27 +235,39 @@ reduce_residual_norm_kernel(const float* __restrict__ part, int splits, int M, i
   for (int i = 0; i < 8; ++i) total += red[i];
   const float r = 1.0f / sqrtf(total / float(N) + eps);
 #pragma unroll
-  for (int t = 0; t < kMaxPer; ++t) {
-    const int n = threadIdx.x + t * 256;
-    if (n < N) y_out[int64_t(m) * N + n] = __float2bfloat16_rn(h[t] * r * bf(w[n]));
+  for (int t = 0; t < kPer; ++t) {
+    const int n = (threadIdx.x + t * 256) * 4;
+    if (n < N) {
+      const uint2 wv = *reinterpret_cast<const uint2*>(w + n);
+      *reinterpret_cast<uint2*>(y_out + int64_t(m) * N + n) = make_uint2(
+          pack_bf16x2(h[t].x * r * __uint_as_float(wv.x << 16),
+                      h[t].y * r * __uint_as_float(wv.x & 0xFFFF0000u)),
+          pack_bf16x2(h[t].z * r * __uint_as_float(wv.y << 16),
+                      h[t].w * r * __uint_as_float(wv.y & 0xFFFF0000u)));
+    }
   }
 }
 
 // act[m, j] = silu(g) * u with g = column j and u = column j + I of the summed
 // gate|up partials (N = 2 I); silu(g) = g / (1 + e^-g) (qwen_megakernel.py:212-216).
+// Four columns per thread; I % 4 == 0.
 __global__ void __launch_bounds__(256)
 swiglu_kernel(const float* __restrict__ part, int splits, int M, int I,
               __nv_bfloat16* __restrict__ act) {
-  const int64_t idx = int64_t(blockIdx.x) * 256 + threadIdx.x;
-  if (idx >= int64_t(M) * I) return;
-  const int m = int(idx / I), j = int(idx % I);
-  float g = 0.f, u = 0.f;
+  const int64_t q = int64_t(blockIdx.x) * 256 + threadIdx.x;  // float4 group index
+  if (q * 4 >= int64_t(M) * I) return;
+  const int m = int(q * 4 / I), j = int(q * 4 % I);
+  float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
   for (int s = 0; s < splits; ++s) {
     const float* p = part + (int64_t(s) * M + m) * (2 * I);
-    g += p[j];
-    u += p[j + I];
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p + j));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p + j + I));
+    g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+    u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
   }
-  act[idx] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+  auto sw = [](float gg, float uu) { return gg / (1.0f + __expf(-gg)) * uu; };
+  *reinterpret_cast<uint2*>(act + q * 4) = make_uint2(pack_bf16x2(sw(g.x, u.x), sw(g.y, u.y)),
+                                                     pack_bf16x2(sw(g.z, u.z), sw(g.w, u.w)));
 }
 
 // ============================================================================ decode attention
@@ -251,6 +275,17 @@ constexpr int DA_D = 64;
 constexpr int DA_GMAX = 8;         // query heads per kv head
 constexpr int DA_CHUNK = 1024;     // keys per CTA at most
 constexpr int DA_THREADS = 128;
+
+// d = a * b + c on two fp32 lanes at once (sm_100 packed FMA).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -300,10 +335,15 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
       }
     }
     for (int g = 0; g < G; ++g) {
-      float s = 0.f;
+      const float4* q4 = reinterpret_cast<const float4*>(sq[g]);
+      float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int d = 0; d < DA_D; ++d) s = fmaf(sq[g][d], kf[d], s);
-      sp[g][j] = s;
+      for (int i = 0; i < DA_D / 4; ++i) {
+        const float4 qq = q4[i];
+        acc = ffma2(make_float2(qq.x, qq.y), make_float2(kf[4 * i], kf[4 * i + 1]), acc);
+        acc = ffma2(make_float2(qq.z, qq.w), make_float2(kf[4 * i + 2], kf[4 * i + 3]), acc);
+      }
+      sp[g][j] = acc.x + acc.y;
     }
   }
   __syncthreads();
@@ -327,24 +367,31 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
     }
   }
   __syncthreads();
-  // Phase 3: o[g, d] for d = tid % 64, heads g = tid / 64 + 2 i.
-  const int d = tid & (DA_D - 1), g0 = tid / DA_D;
-  float acc[DA_GMAX / 2];
+  // Phase 3: o[g, 2c .. 2c+1] for c = tid % 32 and heads g = tid / 32 + 4 i; each step
+  // reads one bf16 pair of V (a warp covers one 128-byte V row).
+  const int c = tid & 31, g0 = tid >> 5;
+  float2 acc[DA_GMAX / 4];
 #pragma unroll
-  for (int i = 0; i < DA_GMAX / 2; ++i) acc[i] = 0.f;
+  for (int i = 0; i < DA_GMAX / 4; ++i) acc[i] = make_float2(0.f, 0.f);
+  const uint32_t* v32 = reinterpret_cast<const uint32_t*>(vbase) + c;
+#pragma unroll 4
   for (int j = 0; j < n; ++j) {
-    const float v = bf(vbase[int64_t(j) * DA_D + d]);
+    const uint32_t vv = __ldg(v32 + j * (DA_D / 2));
+    const float2 v = make_float2(__uint_as_float(vv << 16), __uint_as_float(vv & 0xFFFF0000u));
 #pragma unroll
-    for (int i = 0; i < DA_GMAX / 2; ++i) {
-      const int g = g0 + 2 * i;
-      if (g < G) acc[i] = fmaf(sp[g][j], v, acc[i]);
+    for (int i = 0; i < DA_GMAX / 4; ++i) {
+      const int g = g0 + 4 * i;
+      if (g < G) {
+        const float pp = sp[g][j];
+        acc[i] = ffma2(make_float2(pp, pp), v, acc[i]);
+      }
     }
   }
   const int64_t base = (int64_t(bhk) * nsplit + split) * G;
 #pragma unroll
-  for (int i = 0; i < DA_GMAX / 2; ++i) {
-    const int g = g0 + 2 * i;
-    if (g < G) opart[(base + g) * DA_D + d] = acc[i];
+  for (int i = 0; i < DA_GMAX / 4; ++i) {
+    const int g = g0 + 4 * i;
+    if (g < G) *reinterpret_cast<float2*>(opart + (base + g) * DA_D + 2 * c) = acc[i];
   }
   if (tid < G) {
     mlpart[(base + tid) * 2] = sml[tid][0];
@@ -386,11 +433,11 @@ namespace {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Split-K factor: enough (tile, split) CTAs for ~2 per SM, at least 2 k-blocks per split.
+// Split-K factor: about one (tile, split) CTA per SM, at least 2 k-blocks per split.
 int pick_splits(int64_t N, int64_t K, int sms) {
   const int64_t tiles = (N + SK_BN - 1) / SK_BN;
   const int64_t kbs = (K + SK_BK - 1) / SK_BK;
-  int64_t s = (2 * int64_t(sms) + tiles - 1) / tiles;
+  int64_t s = (int64_t(sms) + tiles - 1) / tiles;
   s = std::min<int64_t>(s, std::max<int64_t>(1, kbs / 2));
   return int(std::max<int64_t>(1, s));
 }
@@ -505,7 +552,7 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
   // 8-9. gate|up projection, SwiGLU
   sp = pick_splits(2 * I, H, sms);
   ENIGMA_TRY(splitk_gemm(bfp(l.h1n), d.w_gate_up, part, B, 2 * I, H, sp, status, s));
-  swiglu_kernel<<<unsigned((int64_t(B) * I + 255) / 256), 256, 0, s>>>(part, sp, B, I, bfp(l.act));
+  swiglu_kernel<<<unsigned((int64_t(B) * I / 4 + 255) / 256), 256, 0, s>>>(part, sp, B, I, bfp(l.act));
   ENIGMA_TRY(cudaGetLastError());
   // 10-11. down projection + residual(h1) -> out
   sp = pick_splits(H, I, sms);

@@ -67,14 +67,16 @@ __device__ __forceinline__ uint4 pack<__nv_bfloat16>(const float* f) {
                     pack_bf16x2(f[6], f[7]));
 }
 
-// THREADS threads per row, NV 16-byte vectors per thread; hidden == THREADS*NV*VE.
-template <typename T, int THREADS, int NV>
+// THREADS threads per row, NV 16-byte vectors per thread.  Without PRED the row is
+// exactly THREADS*NV vectors; with PRED it has row_vecs <= THREADS*NV vectors and the
+// vectors past the end are skipped (e.g. hidden 896 bf16 = 112 vectors on 128 threads).
+template <typename T, int THREADS, int NV, bool PRED = false>
 __global__ void __launch_bounds__(THREADS)
 rmsnorm_row_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
-                   int64_t rows, float inv_hidden, float eps) {
+                   int64_t rows, float inv_hidden, float eps, int row_vecs) {
   constexpr int VE = Vec<T>::kElems;
   constexpr int kWarps = THREADS / 32;
-  constexpr int64_t kRowVecs = int64_t(THREADS) * NV;
+  const int64_t kRowVecs = PRED ? row_vecs : int64_t(THREADS) * NV;
   __shared__ float red[kWarps];
 
   const int tid = threadIdx.x;
@@ -85,7 +87,9 @@ rmsnorm_row_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restri
 
     uint4 raw[NV];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) raw[i] = ld_stream(xv + tid + i * THREADS);
+    for (int i = 0; i < NV; ++i)
+      raw[i] = (!PRED || tid + i * THREADS < kRowVecs) ? ld_stream(xv + tid + i * THREADS)
+                                                       : make_uint4(0u, 0u, 0u, 0u);
 
     float ss = 0.f;
     float f[NV][VE];
@@ -107,6 +111,7 @@ rmsnorm_row_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restri
     const float scale = 1.0f / sqrtf(total * inv_hidden + eps);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
+      if (PRED && tid + i * THREADS >= kRowVecs) continue;
       float wf[VE];
       unpack<T>(__ldg(wv + tid + i * THREADS), wf);
       float o[VE];
@@ -155,15 +160,15 @@ rmsnorm_generic_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __re
   }
 }
 
-template <typename T, int THREADS, int NV>
+template <typename T, int THREADS, int NV, bool PRED = false>
 cudaError_t launch_row(const void* x, const void* w, void* y, int64_t rows, int64_t hidden,
                        float eps, int sms, cudaStream_t s) {
   // Enough CTAs to fill every SM several times over; each CTA strides over rows.
   const int64_t max_ctas = int64_t(sms) * (2048 / THREADS) * 8;
   const int grid = int(rows < max_ctas ? rows : max_ctas);
-  rmsnorm_row_kernel<T, THREADS, NV><<<grid, THREADS, 0, s>>>(
+  rmsnorm_row_kernel<T, THREADS, NV, PRED><<<grid, THREADS, 0, s>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), static_cast<T*>(y), rows,
-      1.0f / float(hidden), eps);
+      1.0f / float(hidden), eps, int(hidden / Vec<T>::kElems));
   return cudaGetLastError();
 }
 
@@ -185,7 +190,13 @@ cudaError_t dispatch(const void* x, const void* w, void* y, int64_t rows, int64_
       case 512:  return launch_row<T, 128, 4>(x, w, y, rows, hidden, eps, sms, s);
       case 1024: return launch_row<T, 256, 4>(x, w, y, rows, hidden, eps, sms, s);
       case 2048: return launch_row<T, 256, 8>(x, w, y, rows, hidden, eps, sms, s);
-      default: break;
+      default:
+        if (vecs <= 128) return launch_row<T, 128, 1, true>(x, w, y, rows, hidden, eps, sms, s);
+        if (vecs <= 256) return launch_row<T, 128, 2, true>(x, w, y, rows, hidden, eps, sms, s);
+        if (vecs <= 512) return launch_row<T, 128, 4, true>(x, w, y, rows, hidden, eps, sms, s);
+        if (vecs <= 1024) return launch_row<T, 256, 4, true>(x, w, y, rows, hidden, eps, sms, s);
+        if (vecs <= 2048) return launch_row<T, 256, 8, true>(x, w, y, rows, hidden, eps, sms, s);
+        break;
     }
   }
   const int64_t max_ctas = int64_t(sms) * 16;

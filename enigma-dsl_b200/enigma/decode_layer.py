@@ -132,6 +132,21 @@ class DecodeLayer:
             self.desc.position = self.position
         return out
 
+    def capture(self, x, out):
+        """Record one step (fixed x / out buffers, current position) as a CUDA graph and
+        return a function that replays it: the step's 11 launches become one submission."""
+        import torch
+        side = torch.cuda.Stream(device=x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):
+            self.step(x, out=out)            # first launches happen outside capture
+        torch.cuda.current_stream(x.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.step(x, out=out)
+        self._graph = graph                  # keep alive
+        return graph.replay
+
     def weight_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in self.w.values())
 

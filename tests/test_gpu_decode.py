@@ -68,3 +68,17 @@ def test_decode_rejects_bad_desc(cuda):
     layer.desc.head_dim = 128
     with pytest.raises(_native.EnigmaCudaError, match="head_dim must be 64"):
         layer.step(__import__("torch").zeros(2, 128, device="cuda").bfloat16())
+
+
+def test_decode_graph_replay_matches(cuda):
+    import torch
+    from enigma.decode_layer import DecodeConfig, DecodeLayer
+    layer = DecodeLayer.random(DecodeConfig(batch=8, hidden=256, heads_q=4, heads_kv=1,
+                                            intermediate=512, cache_len=50, cache_capacity=64))
+    x = torch.randn(8, 256, device="cuda").bfloat16()
+    eager = layer.step(x).float().cpu().numpy()
+    out = torch.empty_like(x)
+    replay = layer.capture(x, out)
+    replay()
+    torch.cuda.synchronize()
+    assert orc.max_abs(out.float().cpu().numpy(), eager) == 0.0
