@@ -293,109 +293,165 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-// One CTA per (sequence b, kv head, key chunk): scores of the G query heads of the
-// group against the chunk's keys (log2 domain), per-head max / sum, then
-// o[g, :] = sum_k p[g, k] V[k, :].  Writes unnormalised partials for the combine.
-//   q      [B, Hq, D] bf16 (RoPE applied), kc / vc [B, Hkv, cap, D] bf16, L keys valid
-//   opart  [B*Hkv, nsplit, G, D] fp32, mlpart [B*Hkv, nsplit, G, 2] fp32 (max, sum)
-__global__ void __launch_bounds__(DA_THREADS)
+// Split-KV decode attention on the tensor cores (mma.sync m16n8k16, bf16 -> fp32).
+// CTA = (sequence b, kv head, key chunk); each of its 4 warps owns a contiguous quarter
+// of the chunk and writes its own unnormalised partial (max, sum, o) for the G <= 8
+// query heads of the group; the combine kernel merges all partials.
+//
+// Per 64-key block a warp computes S = Q K^T (Q = the group's heads as the 16-row A
+// operand, rows >= G zero; K as the B operand straight from global memory), an online
+// softmax in the log2 domain, and O += P V with P taken from the S accumulators and V
+// staged through shared memory (cp.async, XOR-swizzled rows) and read by ldmatrix.trans.
+// The head dimension is consumed in a permuted order: for k-step ks, lane quad t holds
+// fragment columns {2t, 2t+1, 2t+8, 2t+9} = physical dims 16t + 4ks + {0..3}, applied to
+// both Q and K (a dot product is order-free), so each lane reads its K row slice as two
+// contiguous 16-byte loads.
+//   q [B, Hq, D] bf16 (RoPE applied); kc / vc [B, Hkv, cap, D] bf16; L keys valid
+//   opart [B*Hkv, parts, G, D] fp32, mlpart [B*Hkv, parts, G, 2] (max in log2 units, sum)
+constexpr int DA_WARPS = 4;
+constexpr int DA_BLOCK = 64;       // keys per inner step
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
+}
+
+__global__ void __launch_bounds__(DA_WARPS * 32)
 decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
                          const __nv_bfloat16* __restrict__ vc, float* __restrict__ opart,
                          float* __restrict__ mlpart, int Hq, int Hkv, int cap, int L, int chunk,
                          float scale_log2) {
-  __shared__ float sq[DA_GMAX][DA_D];
-  __shared__ float sp[DA_GMAX][DA_CHUNK];
-  __shared__ float sml[DA_GMAX][2];
+  __shared__ __align__(128) uint8_t sv[DA_WARPS][DA_BLOCK * DA_D * 2];   // 8 KB per warp
   const int G = Hq / Hkv;
-  const int bhk = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
+  const int bhk = blockIdx.x, split = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int parts = gridDim.y * DA_WARPS, part = split * DA_WARPS + warp;
   const int b = bhk / Hkv, kvh = bhk % Hkv;
-  const int k0 = split * chunk;
-  const int n = max(0, min(chunk, L - k0));
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int per_warp = (chunk + DA_WARPS - 1) / DA_WARPS;
+  const int k0 = split * chunk + warp * per_warp;
+  const int k1 = min(L, min(split * chunk + chunk, k0 + per_warp));
 
-  for (int i = tid; i < G * DA_D; i += DA_THREADS)
-    sq[i / DA_D][i % DA_D] = bf(q[(int64_t(b) * Hq + kvh * G + i / DA_D) * DA_D + i % DA_D]) *
-                             scale_log2;
-  __syncthreads();
+  // Q fragments (A operand): row g = head g of the group (rows >= G and rows 8..15 zero).
+  uint32_t qa[4][4];
+  {
+    const bool live = g < G;
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+        q + (int64_t(b) * Hq + kvh * G + (live ? g : 0)) * DA_D + 16 * t);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      qa[ks][0] = live ? qrow[2 * ks] : 0u;
+      qa[ks][2] = live ? qrow[2 * ks + 1] : 0u;
+      qa[ks][1] = 0u;
+      qa[ks][3] = 0u;
+    }
+  }
+  const __nv_bfloat16* kbase = kc + int64_t(bhk) * cap * DA_D;
+  const __nv_bfloat16* vbase = vc + int64_t(bhk) * cap * DA_D;
+  const uint32_t sv_addr = smem_u32(sv[warp]);
 
-  const __nv_bfloat16* kbase = kc + (int64_t(bhk) * cap + k0) * DA_D;
-  const __nv_bfloat16* vbase = vc + (int64_t(bhk) * cap + k0) * DA_D;
-  // Phase 1: scores, one key per thread per step; each thread reads its key row (128 B).
-  for (int j = tid; j < n; j += DA_THREADS) {
-    float kf[DA_D];
-    const uint4* kr = reinterpret_cast<const uint4*>(kbase + int64_t(j) * DA_D);
+  float o[8][4];
 #pragma unroll
-    for (int v = 0; v < DA_D / 8; ++v) {
-      const uint4 w = __ldg(kr + v);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;   // row g, log2 units
+
+  for (int kb = k0; kb < k1; kb += DA_BLOCK) {
+    const int nk = min(DA_BLOCK, k1 - kb);
+    // V block -> shared memory: row r (key), 16-byte chunk c stored at chunk c ^ (r & 7).
+    __syncwarp();
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        kf[v * 8 + 2 * e] = __uint_as_float(ws[e] << 16);
-        kf[v * 8 + 2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
+    for (int i = 0; i < (DA_BLOCK * 8) / 32; ++i) {
+      const int idx = i * 32 + lane, r = idx >> 3, c = idx & 7;
+      const int key = kb + min(r, nk - 1);
+      cp_async16(sv_addr + r * 128 + ((c ^ (r & 7)) << 4), vbase + int64_t(key) * DA_D + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+
+    // S = Q K^T for 8 blocks of 8 keys; lane (g, t) loads key kb + 8 nb + g, dims 16t..16t+15.
+    float sacc[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+      const int key = kb + min(nb * 8 + g, nk - 1);
+      const uint4* kr = reinterpret_cast<const uint4*>(kbase + int64_t(key) * DA_D + 16 * t);
+      const uint4 lo = __ldg(kr), hi = __ldg(kr + 1);
+      const uint32_t kw[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) mma_bf16_16816(sacc[nb], qa[ks], kw[2 * ks], kw[2 * ks + 1]);
+    }
+    // Online softmax on row g (columns 2t, 2t+1 of each 8-key block).
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool ok = nb * 8 + 2 * t + e < nk;
+        sacc[nb][e] = ok ? sacc[nb][e] * scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sacc[nb][e]);
       }
     }
-    for (int g = 0; g < G; ++g) {
-      const float4* q4 = reinterpret_cast<const float4*>(sq[g]);
-      float2 acc = make_float2(0.f, 0.f);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = ex2f(m_run - m_new);   // 0 on the first block (m_run = -inf)
+    m_run = m_new;
+    float psum = 0.f;
+    uint32_t pa[8];
 #pragma unroll
-      for (int i = 0; i < DA_D / 4; ++i) {
-        const float4 qq = q4[i];
-        acc = ffma2(make_float2(qq.x, qq.y), make_float2(kf[4 * i], kf[4 * i + 1]), acc);
-        acc = ffma2(make_float2(qq.z, qq.w), make_float2(kf[4 * i + 2], kf[4 * i + 3]), acc);
-      }
-      sp[g][j] = acc.x + acc.y;
+    for (int nb = 0; nb < 8; ++nb) {
+      const float p0 = ex2f(sacc[nb][0] - m_new), p1 = ex2f(sacc[nb][1] - m_new);
+      psum += p0 + p1;
+      pa[nb] = pack_bf16x2(p0, p1);
     }
-  }
-  __syncthreads();
-  // Phase 2: per-head max and sum; p replaces the score.
-  for (int g = warp; g < G; g += DA_THREADS / 32) {
-    float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, sp[g][j]);
+    l_run = l_run * corr + psum;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const float p = ex2f(sp[g][j] - m);
-      sp[g][j] = p;
-      l += p;
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= corr;
+      o[i][1] *= corr;
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+    // O += P V: k-step kk covers keys 16 kk .. 16 kk + 15 (S blocks 2 kk and 2 kk + 1).
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) {
-      sml[g][0] = m;
-      sml[g][1] = l;
-    }
-  }
-  __syncthreads();
-  // Phase 3: o[g, 2c .. 2c+1] for c = tid % 32 and heads g = tid / 32 + 4 i; each step
-  // reads one bf16 pair of V (a warp covers one 128-byte V row).
-  const int c = tid & 31, g0 = tid >> 5;
-  float2 acc[DA_GMAX / 4];
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t a[4] = {pa[2 * kk], 0u, pa[2 * kk + 1], 0u};
 #pragma unroll
-  for (int i = 0; i < DA_GMAX / 4; ++i) acc[i] = make_float2(0.f, 0.f);
-  const uint32_t* v32 = reinterpret_cast<const uint32_t*>(vbase) + c;
-#pragma unroll 4
-  for (int j = 0; j < n; ++j) {
-    const uint32_t vv = __ldg(v32 + j * (DA_D / 2));
-    const float2 v = make_float2(__uint_as_float(vv << 16), __uint_as_float(vv & 0xFFFF0000u));
-#pragma unroll
-    for (int i = 0; i < DA_GMAX / 4; ++i) {
-      const int g = g0 + 4 * i;
-      if (g < G) {
-        const float pp = sp[g][j];
-        acc[i] = ffma2(make_float2(pp, pp), v, acc[i]);
+      for (int nb2 = 0; nb2 < 4; ++nb2) {   // dims 16 nb2 .. 16 nb2 + 15 (two n-blocks)
+        const int mi = lane >> 3, r = 16 * kk + (mi & 1) * 8 + (lane & 7);
+        const int c = 2 * nb2 + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_trans(sv_addr + r * 128 + ((c ^ (r & 7)) << 4), b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * nb2], a, b0, b1);
+        mma_bf16_16816(o[2 * nb2 + 1], a, b2, b3);
       }
     }
   }
-  const int64_t base = (int64_t(bhk) * nsplit + split) * G;
+  // Row sums: each lane holds 16 of the block's 64 columns per step.
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if (g < G) {
+    const int64_t base = (int64_t(bhk) * parts + part) * G + g;
 #pragma unroll
-  for (int i = 0; i < DA_GMAX / 4; ++i) {
-    const int g = g0 + 4 * i;
-    if (g < G) *reinterpret_cast<float2*>(opart + (base + g) * DA_D + 2 * c) = acc[i];
-  }
-  if (tid < G) {
-    mlpart[(base + tid) * 2] = sml[tid][0];
-    mlpart[(base + tid) * 2 + 1] = sml[tid][1];
+    for (int i = 0; i < 8; ++i)
+      *reinterpret_cast<float2*>(opart + base * DA_D + 8 * i + 2 * t) = make_float2(o[i][0], o[i][1]);
+    if (t == 0) {
+      mlpart[base * 2] = m_run;
+      mlpart[base * 2 + 1] = l_run;
+    }
   }
 }
 
@@ -479,8 +535,8 @@ Layout plan(const enigma_decode_layer_desc& d, int sms) {
   l.h1 = take(size_t(B * H) * 2);
   l.h1n = take(size_t(B * H) * 2);
   l.act = take(size_t(B * I) * 2);
-  l.opart = take(size_t(B * Hkv * splits * G * D) * 4);
-  l.mlpart = take(size_t(B * Hkv * splits * G * 2) * 4);
+  l.opart = take(size_t(B * Hkv * splits * DA_WARPS * G * D) * 4);
+  l.mlpart = take(size_t(B * Hkv * splits * DA_WARPS * G * 2) * 4);
   l.total = off;
   return l;
 }
@@ -532,7 +588,7 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
       int(d.cache_capacity), int(d.position));
   ENIGMA_TRY(cudaGetLastError());
   // 4-5. attention over position + 1 keys, split-KV then combine
-  decode_attn_split_kernel<<<dim3(B * Hkv, l.attn_splits), DA_THREADS, 0, s>>>(
+  decode_attn_split_kernel<<<dim3(B * Hkv, l.attn_splits), DA_WARPS * 32, 0, s>>>(
       bfp(l.q), static_cast<const __nv_bfloat16*>(d.k_cache),
       static_cast<const __nv_bfloat16*>(d.v_cache), reinterpret_cast<float*>(w + l.opart),
       reinterpret_cast<float*>(w + l.mlpart), Hq, Hkv, int(d.cache_capacity),
@@ -540,7 +596,7 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
   ENIGMA_TRY(cudaGetLastError());
   decode_attn_combine_kernel<<<B * Hq, DA_D, 0, s>>>(reinterpret_cast<float*>(w + l.opart),
                                                       reinterpret_cast<float*>(w + l.mlpart),
-                                                      bfp(l.attn), Hq, Hkv, l.attn_splits);
+                                                      bfp(l.attn), Hq, Hkv, l.attn_splits * DA_WARPS);
   ENIGMA_TRY(cudaGetLastError());
   // 6-7. O projection + residual(x) -> h1, post-attention RMSNorm -> h1n
   sp = pick_splits(H, Hq * D, sms);
