@@ -34,7 +34,7 @@ using namespace enigma_sm100;
 constexpr int SK_BM = 128;
 constexpr int SK_BN = 64;
 constexpr int SK_BK = 64;
-constexpr int SK_STAGES = 4;
+constexpr int SK_STAGES = 8;
 constexpr int SK_A_BYTES = SK_BM * SK_BK * 2;   // 16 KB
 constexpr int SK_B_BYTES = SK_BK * SK_BN * 2;   // 8 KB
 constexpr int SK_STAGE = SK_A_BYTES + SK_B_BYTES;
@@ -272,9 +272,6 @@ swiglu_kernel(const float* __restrict__ part, int splits, int M, int I,
 
 // ============================================================================ decode attention
 constexpr int DA_D = 64;
-constexpr int DA_GMAX = 8;         // query heads per kv head
-constexpr int DA_CHUNK = 1024;     // keys per CTA at most
-constexpr int DA_THREADS = 128;
 
 // d = a * b + c on two fp32 lanes at once (sm_100 packed FMA).
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
@@ -456,26 +453,48 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
 }
 
 // out[b, h*D + d] = sum_s 2^(m_s - M) o_s[d] / sum_s 2^(m_s - M) l_s  (bf16).
+// One CTA of 64 threads per (b, h): the first warp reduces the partials' maxima and sums
+// (lane s owns partial s, parts <= 64), the weights go to shared memory, then every
+// thread sums its dim over the partials with independent loads.
 __global__ void __launch_bounds__(DA_D)
 decode_attn_combine_kernel(const float* __restrict__ opart, const float* __restrict__ mlpart,
-                           __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int nsplit) {
+                           __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int nparts) {
+  __shared__ float wgt[64];
+  __shared__ float inv_den;
   const int G = Hq / Hkv;
   const int bh = blockIdx.x;            // b * Hq + h
   const int b = bh / Hq, h = bh % Hq;
   const int bhk = b * Hkv + h / G, g = h % G;
-  const int d = threadIdx.x;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, mlpart[((int64_t(bhk) * nsplit + s) * G + g) * 2]);
-  float num = 0.f, den = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const int64_t i = (int64_t(bhk) * nsplit + s) * G + g;
-    const float m = mlpart[i * 2];
-    if (m == -INFINITY) continue;
-    const float w = ex2f(m - M);
-    num = fmaf(w, opart[i * DA_D + d], num);
-    den = fmaf(w, mlpart[i * 2 + 1], den);
+  const int tid = threadIdx.x;
+  if (tid < 32) {
+    float m[2], l[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int s = tid + 32 * k;
+      const int64_t i = (int64_t(bhk) * nparts + s) * G + g;
+      m[k] = s < nparts ? mlpart[i * 2] : -INFINITY;
+      l[k] = s < nparts ? mlpart[i * 2 + 1] : 0.f;
+    }
+    float M = fmaxf(m[0], m[1]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float den = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float w = (m[k] == -INFINITY) ? 0.f : ex2f(m[k] - M);
+      wgt[tid + 32 * k] = w;
+      den = fmaf(w, l[k], den);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (tid == 0) inv_den = den > 0.f ? 1.0f / den : 0.f;
   }
-  out[int64_t(bh) * DA_D + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+  __syncthreads();
+  const float* op = opart + (int64_t(bhk) * nparts * G + g) * DA_D + tid;
+  float num = 0.f;
+#pragma unroll 4
+  for (int s = 0; s < nparts; ++s) num = fmaf(wgt[s], __ldg(op + int64_t(s) * G * DA_D), num);
+  out[int64_t(bh) * DA_D + tid] = __float2bfloat16_rn(num * inv_den);
 }
 
 }  // namespace
@@ -511,20 +530,14 @@ Layout plan(const enigma_decode_layer_desc& d, int sms) {
   int64_t part = 0;
   for (auto& g : gemms) part = std::max(part, pick_splits(g[0], g[1], sms) * B * g[0]);
   Layout l;
-  // Split the keys so (sequence, kv head, chunk) CTAs cover ~4 per SM; chunks hold at most
-  // DA_CHUNK keys.  The workspace is sized for the largest split count any position up to
-  // the cache capacity can need, so one workspace serves every step.
-  const int64_t target = std::max<int64_t>(1, (4 * int64_t(sms) + B * Hkv - 1) / (B * Hkv));
-  auto split_for = [&](int64_t keys, int64_t* chunk_out) {
-    int64_t sp = std::max<int64_t>(target, (keys + DA_CHUNK - 1) / DA_CHUNK);
-    int64_t ch = (keys + sp - 1) / sp;
-    if (chunk_out) *chunk_out = ch;
-    return (keys + ch - 1) / ch;
-  };
-  int64_t chunk = 0;
-  l.attn_splits = int(split_for(L, &chunk));
+  // Split the keys so (sequence, kv head, chunk) CTAs cover ~4 per SM, at most 16 chunks
+  // (4 warp partials each; the combine kernel takes up to 64 partials).  The workspace is
+  // sized for that maximum, so one workspace serves every position.
+  const int64_t splits = std::min<int64_t>(
+      16, std::max<int64_t>(1, (4 * int64_t(sms) + B * Hkv - 1) / (B * Hkv)));
+  const int64_t chunk = (L + splits - 1) / splits;
+  l.attn_splits = int((L + chunk - 1) / chunk);
   l.attn_chunk = int(chunk);
-  const int64_t splits = std::max<int64_t>(target, (d.cache_capacity + DA_CHUNK - 1) / DA_CHUNK);
   const int64_t G = Hq / Hkv;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align256(off + bytes); return o; };
