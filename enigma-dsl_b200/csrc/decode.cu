@@ -34,7 +34,7 @@ using namespace enigma_sm100;
 constexpr int SK_BM = 128;
 constexpr int SK_BN = 64;
 constexpr int SK_BK = 64;
-constexpr int SK_STAGES = 8;
+constexpr int SK_STAGES = 4;
 constexpr int SK_A_BYTES = SK_BM * SK_BK * 2;   // 16 KB
 constexpr int SK_B_BYTES = SK_BK * SK_BN * 2;   // 8 KB
 constexpr int SK_STAGE = SK_A_BYTES + SK_B_BYTES;
