@@ -4,24 +4,31 @@
 //
 // The reference computes the same thing with an online softmax over KV tiles
 // on Apple SIMD groups (examples/benchmark_sdpa.py:48-150,
-// examples/showcase_attention.py:31-91, check at :150-153).  Here each CTA owns
-// one 128-row Q tile of one (batch, head) and streams 128-key K/V tiles:
+// examples/showcase_attention.py:31-91, check at :150-153).
 //
-//   warp 0     TMA: Q once; K and V tiles into 2-stage rings (128B swizzle,
-//              3-D tensor maps [D, S, B*H] so ragged S edges zero-fill and
-//              never read the next head).  No multicast.
-//   warp 1     one lane issues tcgen05.mma:
-//                S_j = Q K_j^T      (SS, M128 N128, fp32 in TMEM, 2 buffers)
-//                O  += P_j V_j      (TS: P read from TMEM, V MN-major from smem)
-//              in the order S_0, S_1, PV_0, S_2, PV_1, ... so the tensor core
-//              computes S_{j+1} and PV_{j-1} while the softmax works on S_j.
-//   warps 2-5  softmax, one thread per Q row: tcgen05.ld the S row, mask,
-//              running max in the log2 domain, p = 2^(x - m) with ex2.approx,
-//              row sum, P packed to bf16 and stored with tcgen05.st over the
-//              first half of S's own columns.  O is rescaled only when the
-//              running max grows by more than 8 (a factor 256), which keeps the
-//              result exact (numerator and denominator share the stale max)
-//              and makes the TMEM read-modify-write of O rare.
+// One CTA owns two 128-row Q tiles (Q0, Q1) of one (batch, head) and streams
+// 128-key K/V tiles past both:
+//
+//   warp 0      TMA: Q0, Q1 once; K and V tiles into 2-stage rings (128B swizzle,
+//               3-D tensor maps [D, S, B*H]: ragged S zero-fills and never reads
+//               the next head).  No multicast.
+//   warp 1      one lane issues tcgen05.mma (fp32 accumulators in TMEM):
+//                 S_i = Q_i K_j^T   (SS, M128 N128)          i = 0, 1
+//                 O_i += P_i V_j    (TS: P read from TMEM over S_i's columns)
+//               in the order S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 ...
+//               so the tensor core works on one tile's S / PV while the other
+//               tile's softmax runs (ping-pong).  Because tcgen05.commit tracks
+//               every earlier MMA of the issuing thread, "S_i(j) done" also means
+//               "PV_i(j-1) done": the softmax may touch O_i after that wait.
+//   warps 2-5   softmax of Q0, warps 6-9 softmax of Q1; one thread per row:
+//               tcgen05.ld the S row, row max (3-input max), p = 2^(s*c - m*c)
+//               with packed f32x2 FMAs, row sum, P packed to bf16 and stored with
+//               tcgen05.st over the first half of S's columns.  About 3/8 of the
+//               exponentials run on the FMA pipe (Cody-Waite range reduction and a
+//               degree-4 polynomial, relative error 3.1e-6, fitted by least squares
+//               on Chebyshev nodes) so the MUFU unit is not the bottleneck.  O is
+//               rescaled only when a row max grows by more than 2^8 (exact: the
+//               numerator and denominator share the stale max).
 // All mbarrier waits are bounded (sm100.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -32,35 +39,79 @@ namespace {
 
 using namespace enigma_sm100;
 
-constexpr int BM = 128;            // query rows per CTA
+constexpr int BM = 128;            // rows per Q tile (two tiles per CTA)
 constexpr int BN = 128;            // keys per KV tile
 constexpr int KV_STAGES = 2;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;       // TMA warp, MMA warp, 2 x 4 softmax warps
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+template <int D>
+struct Cfg {
+  static constexpr int Q_BYTES = BM * D * 2;     // one Q tile
+  static constexpr int KV_BYTES = BN * D * 2;    // one K tile == one V tile
+  static constexpr int KATOMS = D / 64;          // 128-byte swizzle atoms along D
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = 512;     // S0 | S1 | O0 | O1
+  static constexpr uint32_t O_COL = 2 * BN;
+};
+
+struct Params {
+  __nv_bfloat16* O;
+  int Sq, Sk, Hq, Hkv, num_ctas_q;
+  float scale_log2;
+  int causal;
+  uint32_t* status;
+};
+
+// ------------------------------------------------------------------ packed fp32 math
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-template <int D>
-struct Cfg {
-  static constexpr int Q_BYTES = BM * D * 2;
-  static constexpr int KV_BYTES = BN * D * 2;   // one K tile == one V tile
-  static constexpr int KATOMS = D / 64;          // 128-byte swizzle atoms along D
-  static constexpr int SMEM = Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 256;
-  static constexpr uint32_t TMEM_COLS = 512;     // S0 | S1 | O (| unused)
-  static constexpr uint32_t O_COL = 2 * BN;
-};
-
-struct Params {
-  __nv_bfloat16* O;
-  int Sq, Sk, Hq, Hkv, num_q_tiles;
-  float scale_log2;
-  int causal;
-  uint32_t* status;
-};
+// 2^x for a pair, on the FMA pipe, for softmax arguments x <= 0.  x < -125 gives 0
+// (so masked -inf entries contribute exactly nothing); otherwise x = n + f with
+// n = round(x) (the 1.5 * 2^23 shifter), f in [-0.5, 0.5], 2^f by a degree-4
+// polynomial and n added to the exponent field (the result stays a normal float).
+__device__ __forceinline__ float2 ex2_poly2(float2 x0) {
+  float2 x = make_float2(fmaxf(x0.x, -125.f), fmaxf(x0.y, -125.f));
+  const float2 shifter = make_float2(12582912.f, 12582912.f);
+  const float2 t = f2add(x, shifter);                       // round to integer in the mantissa
+  const float2 n = f2add(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = f2add(x, make_float2(-n.x, -n.y));
+  float2 p = make_float2(0.00960039533674717f, 0.00960039533674717f);
+  p = f2fma(p, f, make_float2(0.05591689422726631f, 0.05591689422726631f));
+  p = f2fma(p, f, make_float2(0.24023719131946564f, 0.24023719131946564f));
+  p = f2fma(p, f, make_float2(0.6931219696998596f, 0.6931219696998596f));
+  p = f2fma(p, f, make_float2(1.0f, 1.0f));
+  const int ex = __float_as_int(t.x) << 23, ey = __float_as_int(t.y) << 23;
+  return make_float2(x0.x < -125.f ? 0.f : __int_as_float(__float_as_int(p.x) + ex),
+                     x0.y < -125.f ? 0.f : __int_as_float(__float_as_int(p.y) + ey));
+}
 
 template <int D>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -70,33 +121,39 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + C::Q_BYTES;
+  uint8_t* sQ = smem;                                   // Q0 | Q1
+  uint8_t* sK = sQ + 2 * C::Q_BYTES;
   uint8_t* sV = sK + KV_STAGES * C::KV_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KV_STAGES * C::KV_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_full = bars;                   // [1]
+  uint64_t* k_full = q_full + 1;             // [KV_STAGES]
   uint64_t* k_empty = k_full + KV_STAGES;
   uint64_t* v_full = k_empty + KV_STAGES;
   uint64_t* v_empty = v_full + KV_STAGES;
-  uint64_t* s_full = v_empty + KV_STAGES;   // [2]
-  uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* o_done = p_full + 2;            // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  uint64_t* s_full = v_empty + KV_STAGES;    // [2] one per Q tile
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* o_done = p_full + 2;             // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   // Heavy (late, for causal) query tiles first.
-  const int qb = p.num_q_tiles - 1 - int(blockIdx.x);
+  const int pair = p.num_ctas_q - 1 - int(blockIdx.x);
   const int bh = int(blockIdx.y);             // b * Hq + h
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int bhk = b * p.Hkv + h / (p.Hq / p.Hkv);
-  const int q0 = qb * BM;
+  const int q0 = pair * 2 * BM;               // first row of Q0; Q1 starts at q0 + BM
   const int diag = p.Sk - p.Sq;               // key j visible to query i iff j <= i + diag
-  int kv_end = p.Sk;                          // exclusive
-  if (p.causal) kv_end = min(p.Sk, q0 + BM - 1 + diag + 1);
-  const int n_kv = kv_end > 0 ? (kv_end + BN - 1) / BN : 0;
+  int n_kv[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    int end = p.Sk;                                                  // exclusive
+    if (p.causal) end = min(p.Sk, q0 + i * BM + BM - 1 + diag + 1);
+    if (q0 + i * BM >= p.Sq) end = 0;                                // tile entirely past Sq
+    n_kv[i] = end > 0 ? (end + BN - 1) / BN : 0;
+  }
+  const int n_all = max(n_kv[0], n_kv[1]);
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmQ);
@@ -109,11 +166,11 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(o_done, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -127,12 +184,14 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (elect_one() && n_kv > 0) {
-      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+    if (elect_one() && n_all > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
 #pragma unroll
-      for (int a = 0; a < C::KATOMS; ++a)
-        tma_load_3d(sQ + a * BM * 128, &tmQ, q_full, a * 64, q0, bh);
-      for (int j = 0; j < n_kv; ++j) {
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int a = 0; a < C::KATOMS; ++a)
+          tma_load_3d(sQ + i * C::Q_BYTES + a * BM * 128, &tmQ, q_full, a * 64, q0 + i * BM, bh);
+      for (int j = 0; j < n_all; ++j) {
         const int s = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
         if (!mbar_wait(&k_empty[s], ph ^ 1, p.status)) break;
@@ -150,90 +209,103 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0 && n_all > 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(BM, BN, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(BM, D, false, true);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       bool ok = mbar_wait(q_full, 0, p.status);
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % KV_STAGES;
-        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, p.status)) return false;
-        if (!mbar_wait(&v_full[s], (i / KV_STAGES) & 1, p.status)) return false;
+      // S_i(j) = Q_i K_j^T into S buffer i.
+      auto issue_s = [&](int i, int j) {
+        const int s = j % KV_STAGES;
+        const uint32_t s_tmem = tmem + uint32_t(i * BN);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t offq = i * C::Q_BYTES + (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          const uint32_t offk = s * C::KV_BYTES + (kk / 4) * (BN * 128) + (kk % 4) * 32;
+          mma_bf16_ss(s_tmem, smem_desc_sw128(q_addr + offq, 16, 1024),
+                      smem_desc_sw128(k_addr + offk, 16, 1024), idesc_s, kk != 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[i]);
+      };
+      // O_i += P_i(j) V_j, P_i(j) read from TMEM over S buffer i.
+      auto issue_pv = [&](int i, int j) -> bool {
+        const int s = j % KV_STAGES;
+        if (!mbar_wait(&p_full[i], j & 1, p.status)) return false;
+        if (!mbar_wait(&v_full[s], (j / KV_STAGES) & 1, p.status)) return false;
         tc_fence_after();
-        const uint32_t p_tmem = tmem + uint32_t((i & 1) * BN);
+        const uint32_t p_tmem = tmem + uint32_t(i * BN);
         const uint64_t dv = smem_desc_sw128(v_addr + s * C::KV_BYTES, BN * 128, 1024);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_bf16_ts(tmem + C::O_COL, p_tmem + kk * 8, dv + uint64_t((kk * 2048) >> 4), idesc_o,
-                      (i | kk) != 0 ? 1u : 0u);
-        mma_commit(&v_empty[s]);
-        mma_commit(o_done);
+          mma_bf16_ts(tmem + C::O_COL + i * D, p_tmem + kk * 8, dv + uint64_t((kk * 2048) >> 4),
+                      idesc_o, (j | kk) != 0 ? 1u : 0u);
         return true;
       };
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j % KV_STAGES;
-        if (!mbar_wait(&k_full[s], (j / KV_STAGES) & 1, p.status)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t s_tmem = tmem + uint32_t((j & 1) * BN);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk / 4) * (BM * 128) + (kk % 4) * 32;
-          const uint32_t offk = (kk / 4) * (BN * 128) + (kk % 4) * 32;
-          mma_bf16_ss(s_tmem, smem_desc_sw128(q_addr + off, 16, 1024),
-                      smem_desc_sw128(k_addr + s * C::KV_BYTES + offk, 16, 1024), idesc_s,
-                      kk != 0 ? 1u : 0u);
+      for (int j = 0; j <= n_all && ok; ++j) {
+        const bool have_k = j < n_all;
+        if (have_k) {
+          if (!mbar_wait(&k_full[j % KV_STAGES], (j / KV_STAGES) & 1, p.status)) break;
+          tc_fence_after();
         }
-        mma_commit(&k_empty[s]);
-        mma_commit(&s_full[j & 1]);
-        if (j >= 1) ok = issue_pv(j - 1);
+#pragma unroll
+        for (int i = 0; i < 2 && ok; ++i) {
+          if (j >= 1 && j - 1 < n_kv[i]) {
+            ok = issue_pv(i, j - 1);
+            if (ok && j == n_kv[i]) mma_commit(&o_done[i]);
+          }
+          if (ok && have_k && j < n_kv[i]) issue_s(i, j);
+        }
+        if (!ok) break;
+        if (have_k) mma_commit(&k_empty[j % KV_STAGES]);
+        if (j >= 1) mma_commit(&v_empty[(j - 1) % KV_STAGES]);
       }
-      if (ok) issue_pv(n_kv - 1);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax / epilogue
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;        // row of the Q tile owned by this thread
-    const int qi = q0 + r;                    // query index
+    const int ti = (warp - 2) >> 2;           // Q tile of this warpgroup
+    const int quarter = warp & 3;             // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;        // row of the tile owned by this thread
+    const int qi = q0 + ti * BM + r;          // query index
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-    float m_used = -INFINITY, l = 0.f;
+    const uint32_t s_addr = tmem + lane_off + uint32_t(ti * BN);
+    const uint32_t o_addr = tmem + lane_off + C::O_COL + uint32_t(ti * D);
+    const float c = p.scale_log2;
+    const int n_my = n_kv[ti];
+    float m_used = -INFINITY, l = 0.f;        // m in raw score units
     bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status)) { ok = false; break; }
+    for (int j = 0; j < n_my && ok; ++j) {
+      if (!mbar_wait(&s_full[ti], j & 1, p.status)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t s_addr = tmem + lane_off + uint32_t((j & 1) * BN);
       float x[BN];
 #pragma unroll
-      for (int c = 0; c < BN; c += 16) tmem_ld16(s_addr + c, *reinterpret_cast<uint32_t(*)[16]>(&x[c]));
+      for (int k = 0; k < BN; k += 16) tmem_ld16(s_addr + k, *reinterpret_cast<uint32_t(*)[16]>(&x[k]));
       tmem_wait_ld();
-      // Mask keys past the sequence end and, for causal, past this row's diagonal.
+      // Keys past the sequence end and, for causal, past this row's diagonal are masked.
       const int k0 = j * BN;
-      int lim = p.Sk - k0;                                // keys [k0, k0+lim) are valid
+      int lim = p.Sk - k0;
       if (p.causal) lim = min(lim, qi + (p.Sk - p.Sq) - k0 + 1);
-      float mx = -INFINITY;
+      if (lim < BN) {
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        x[c] = (c < lim) ? x[c] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+        for (int k = 0; k < BN; ++k) x[k] = (k < lim) ? x[k] : -INFINITY;
       }
+      float mx = x[0];
+#pragma unroll
+      for (int k = 1; k + 1 < BN; k += 2) mx = max3f(mx, x[k], x[k + 1]);
+      mx = fmaxf(mx, x[BN - 1]);
       const float m_new = fmaxf(m_used, mx);
-      // tcgen05.ld/st are warp-collective, so the rescale decision is taken per warp:
-      // if any row of the warp needs it, every lane rewrites its O row (factor 1
-      // for rows that keep their max).
-      const bool need = (j > 0) && (m_new > m_used + kRescaleThreshold);
+      // tcgen05.ld/st are warp-collective: the lazy-rescale decision is taken per warp.
+      const bool need = (j > 0) && ((m_new - m_used) * c > kRescaleThreshold);
       if (j == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, need)) {
-        // O holds PV_0..PV_{j-1}; wait for PV_{j-1} before rewriting it.
-        if (!mbar_wait(o_done, (j - 1) & 1, p.status)) { ok = false; break; }
-        tc_fence_after();
-        const float f = need ? ex2(m_used - m_new) : 1.0f;  // m_used may be -inf: f = 0
+        // "S_i(j) done" implies PV_i(j-1) done (commit order), so O is complete here.
+        const float f = need ? ex2((m_used - m_new) * c) : 1.0f;   // m_used = -inf: f = 0
         l *= f;
-        const uint32_t o_addr = tmem + lane_off + C::O_COL;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
+        for (int k = 0; k < D; k += 16) {
           uint32_t o[16];
-          tmem_ld16(o_addr + c, o);
+          tmem_ld16(o_addr + k, o);
           tmem_wait_ld();
           uint32_t lo[8], hi[8];
 #pragma unroll
@@ -241,42 +313,49 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             lo[t] = __float_as_uint(__uint_as_float(o[t]) * f);
             hi[t] = __float_as_uint(__uint_as_float(o[8 + t]) * f);
           }
-          tmem_st8(o_addr + c, lo);
-          tmem_st8(o_addr + c + 8, hi);
+          tmem_st8(o_addr + k, lo);
+          tmem_st8(o_addr + k + 8, hi);
         }
         tmem_wait_st();
         if (need) m_used = m_new;
       }
-      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
-      float sum = 0.f;
-      uint32_t pk[BN / 2];
+      const float mc = (m_used == -INFINITY) ? 0.f : m_used * c;
+      const float2 cc = make_float2(c, c), nmc = make_float2(-mc, -mc);
+      float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const float a = ex2(x[c] - m_eff), bb = ex2(x[c + 1] - m_eff);
-        sum += a + bb;
-        pk[c / 2] = pack_bf16x2(a, bb);
+      for (int k = 0; k < BN; k += 16) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float2 y = f2fma(make_float2(x[k + 2 * t], x[k + 2 * t + 1]), cc, nmc);
+          float2 e;
+          if (t >= 5) {
+            e = ex2_poly2(y);                  // 3 of every 8 pairs on the FMA pipe
+          } else {
+            e = make_float2(ex2(y.x), ex2(y.y));
+          }
+          sum2 = f2add(sum2, e);
+          pk[t] = pack_bf16x2(e.x, e.y);
+        }
+        tmem_st8(s_addr + k / 2, pk);          // P (bf16 pairs) over S's first 64 columns
       }
-      l += sum;
-#pragma unroll
-      for (int c = 0; c < BN / 2; c += 8)
-        tmem_st8(s_addr + c, *reinterpret_cast<const uint32_t(*)[8]>(&pk[c]));
+      l += sum2.x + sum2.y;
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
+      mbar_arrive(&p_full[ti]);
     }
     // Epilogue: O / l, bf16, straight to global (each thread one 2*D-byte row).
-    if (ok && n_kv > 0) ok = mbar_wait(o_done, (n_kv - 1) & 1, p.status);
+    if (ok && n_my > 0) ok = mbar_wait(&o_done[ti], 0, p.status);
     if (ok) {
       tc_fence_after();
       const bool live = qi < p.Sq;
-      const float inv = (n_kv > 0 && l > 0.f) ? 1.0f / l : 0.f;
+      const float inv = (n_my > 0 && l > 0.f) ? 1.0f / l : 0.f;
       __nv_bfloat16* orow = p.O + (int64_t(bh) * p.Sq + (live ? qi : 0)) * D;
-      const uint32_t o_addr = tmem + lane_off + C::O_COL;
 #pragma unroll 1
-      for (int c = 0; c < D; c += 16) {
+      for (int k = 0; k < D; k += 16) {
         uint32_t o[16];
-        if (n_kv > 0) {  // CTA-uniform: the warp-collective load runs on every lane
-          tmem_ld16(o_addr + c, o);
+        if (n_my > 0) {  // warp-uniform: the collective load runs on every lane
+          tmem_ld16(o_addr + k, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -292,8 +371,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         w1.z = pack_bf16x2(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv);
         w1.w = pack_bf16x2(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv);
         if (live) {
-          reinterpret_cast<uint4*>(orow + c)[0] = w0;
-          reinterpret_cast<uint4*>(orow + c)[1] = w1;
+          reinterpret_cast<uint4*>(orow + k)[0] = w0;
+          reinterpret_cast<uint4*>(orow + k)[1] = w1;
         }
       }
     }
@@ -350,11 +429,11 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   p.Sk = int(Sk);
   p.Hq = int(Hq);
   p.Hkv = int(Hkv);
-  p.num_q_tiles = int((Sq + BM - 1) / BM);
+  p.num_ctas_q = int((Sq + 2 * BM - 1) / (2 * BM));
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.status = enigma::device_status();
-  dim3 grid(unsigned(p.num_q_tiles), unsigned(B * Hq));
+  dim3 grid(unsigned(p.num_ctas_q), unsigned(B * Hq));
   sdpa_fwd_tc_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
