@@ -42,7 +42,16 @@ using namespace enigma_sm100;
 constexpr int BM = 128;            // rows per Q tile (two tiles per CTA)
 constexpr int BN = 128;            // keys per KV tile
 constexpr int KV_STAGES = 2;
-constexpr int THREADS = 320;       // TMA warp, MMA warp, 2 x 4 softmax warps
+constexpr int THREADS = 384;       // warpgroup 0: TMA warp, MMA warp, 2 idle; WG 1, 2: softmax
+// Register split (setmaxnreg): the kernel launches with LAUNCH_REGS per thread
+// (384 x 168 = 64512 of the SM's 65536); warpgroup 0 gives back down to WG0_REGS and
+// the two softmax warpgroups grow to SOFTMAX_REGS.  128*56 + 256*224 = 64512: the sum
+// equals the launch budget exactly (the host refuses to launch if the compiled kernel
+// has fewer registers than LAUNCH_REGS, since the increase could then never be granted).
+constexpr int LAUNCH_REGS = 168;
+constexpr int WG0_REGS = 56;
+constexpr int SOFTMAX_REGS = 224;
+static_assert(128 * WG0_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
@@ -131,8 +140,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint64_t* v_full = k_empty + KV_STAGES;
   uint64_t* v_empty = v_full + KV_STAGES;
   uint64_t* s_full = v_empty + KV_STAGES;    // [2] one per Q tile
-  uint64_t* p_full = s_full + 2;             // [2]
-  uint64_t* o_done = p_full + 2;             // [2]
+  uint64_t* p_full = s_full + 2;             // [2 tiles][2 halves of the keys]
+  uint64_t* o_done = p_full + 4;             // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5;
@@ -168,7 +177,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[2 * i], 128);
+      mbar_init(&p_full[2 * i + 1], 128);
       mbar_init(&o_done[i], 1);
     }
     fence_barrier_init();
@@ -182,7 +192,9 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp < 4) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(WG0_REGS));
+   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (elect_one() && n_all > 0) {
       mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
@@ -228,17 +240,22 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mma_commit(&s_full[i]);
       };
       // O_i += P_i(j) V_j, P_i(j) read from TMEM over S buffer i.
+      // P arrives in two halves (keys 0-63, 64-127) so the first half's MMAs start while
+      // the softmax finishes the second.
       auto issue_pv = [&](int i, int j) -> bool {
         const int s = j % KV_STAGES;
-        if (!mbar_wait(&p_full[i], j & 1, p.status)) return false;
         if (!mbar_wait(&v_full[s], (j / KV_STAGES) & 1, p.status)) return false;
-        tc_fence_after();
         const uint32_t p_tmem = tmem + uint32_t(i * BN);
         const uint64_t dv = smem_desc_sw128(v_addr + s * C::KV_BYTES, BN * 128, 1024);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          mma_bf16_ts(tmem + C::O_COL + i * D, p_tmem + kk * 8, dv + uint64_t((kk * 2048) >> 4),
-                      idesc_o, (j | kk) != 0 ? 1u : 0u);
+        for (int half = 0; half < 2; ++half) {
+          if (!mbar_wait(&p_full[2 * i + half], j & 1, p.status)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = half * 4; kk < half * 4 + 4; ++kk)
+            mma_bf16_ts(tmem + C::O_COL + i * D, p_tmem + kk * 8,
+                        dv + uint64_t((kk * 2048) >> 4), idesc_o, (j | kk) != 0 ? 1u : 0u);
+        }
         return true;
       };
       for (int j = 0; j <= n_all && ok; ++j) {
@@ -261,9 +278,11 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
     }
     __syncwarp();
+   }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(SOFTMAX_REGS));
     // ------------------------------------------------------------ softmax / epilogue
-    const int ti = (warp - 2) >> 2;           // Q tile of this warpgroup
+    const int ti = (warp - 4) >> 2;           // Q tile of this warpgroup
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;        // row of the tile owned by this thread
     const int qi = q0 + ti * BM + r;          // query index
@@ -289,10 +308,14 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 #pragma unroll
         for (int k = 0; k < BN; ++k) x[k] = (k < lim) ? x[k] : -INFINITY;
       }
-      float mx = x[0];
+      // Row max: four independent 3-input-max chains, then combined.
+      float mq[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-      for (int k = 1; k + 1 < BN; k += 2) mx = max3f(mx, x[k], x[k + 1]);
-      mx = fmaxf(mx, x[BN - 1]);
+      for (int k = 4; k < BN; k += 8) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mq[u] = max3f(mq[u], x[k + u], x[k + 4 + u]);
+      }
+      const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
       const float m_new = fmaxf(m_used, mx);
       // tcgen05.ld/st are warp-collective: the lazy-rescale decision is taken per warp.
       const bool need = (j > 0) && ((m_new - m_used) * c > kRescaleThreshold);
@@ -338,11 +361,13 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           pk[t] = pack_bf16x2(e.x, e.y);
         }
         tmem_st8(s_addr + k / 2, pk);          // P (bf16 pairs) over S's first 64 columns
+        if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
+        }
       }
       l += sum2.x + sum2.y;
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[ti]);
     }
     // Epilogue: O / l, bf16, straight to global (each thread one 2*D-byte row).
     if (ok && n_my > 0) ok = mbar_wait(&o_done[ti], 0, p.status);
@@ -423,6 +448,15 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   cudaError_t e = cudaFuncSetAttribute(sdpa_fwd_tc_kernel<D>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
   if (e != cudaSuccess) return e;
+  static int regs[2] = {-1, -1};
+  int& nreg = regs[D == 128 ? 1 : 0];
+  if (nreg < 0) {
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, sdpa_fwd_tc_kernel<D>);
+    if (e != cudaSuccess) return e;
+    nreg = fa.numRegs;
+  }
+  if (nreg < LAUNCH_REGS) return cudaErrorInvalidConfiguration;  // split could not be granted
   Params p;
   p.O = static_cast<__nv_bfloat16*>(O);
   p.Sq = int(Sq);
