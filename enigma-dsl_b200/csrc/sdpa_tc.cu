@@ -45,12 +45,12 @@ constexpr int KV_STAGES = 2;
 constexpr int THREADS = 384;       // warpgroup 0: TMA warp, MMA warp, 2 idle; WG 1, 2: softmax
 // Register split (setmaxnreg): the kernel launches with LAUNCH_REGS per thread
 // (384 x 168 = 64512 of the SM's 65536); warpgroup 0 gives back down to WG0_REGS and
-// the two softmax warpgroups grow to SOFTMAX_REGS.  128*56 + 256*224 = 64512: the sum
+// the two softmax warpgroups grow to SOFTMAX_REGS.  128*104 + 256*200 = 64512: the sum
 // equals the launch budget exactly (the host refuses to launch if the compiled kernel
 // has fewer registers than LAUNCH_REGS, since the increase could then never be granted).
 constexpr int LAUNCH_REGS = 168;
-constexpr int WG0_REGS = 56;
-constexpr int SOFTMAX_REGS = 224;
+constexpr int WG0_REGS = 104;
+constexpr int SOFTMAX_REGS = 200;
 static_assert(128 * WG0_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
