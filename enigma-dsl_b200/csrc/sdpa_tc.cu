@@ -33,6 +33,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace {
@@ -102,14 +104,14 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x for a pair, on the FMA pipe, for finite softmax arguments x <= 0 (used only on
-// tiles without masked entries).  x is clamped to -126 (2^-126 is negligible next to
-// the row maximum's 1); x = n + f with n = round(x) via the 1.5 * 2^23 shifter,
-// f in [-0.5, 0.5], 2^f by a degree-4 polynomial, and n added to the exponent field
-// with one integer multiply-add (bits(t) * 2^23 keeps exactly n << 23).
+// 2^x for a pair, on the FMA pipe, for softmax arguments x <= 0.  x < -125 gives 0
+// (so masked -inf entries contribute exactly nothing); otherwise x = n + f with
+// n = round(x) (the 1.5 * 2^23 shifter), f in [-0.5, 0.5], 2^f by a degree-4
+// polynomial and n added to the exponent field (the result stays a normal float).
 __device__ __forceinline__ float2 ex2_poly2(float2 x0) {
-  const float2 x = make_float2(fmaxf(x0.x, -126.f), fmaxf(x0.y, -126.f));
-  const float2 t = f2add(x, make_float2(12582912.f, 12582912.f));
+  float2 x = make_float2(fmaxf(x0.x, -125.f), fmaxf(x0.y, -125.f));
+  const float2 shifter = make_float2(12582912.f, 12582912.f);
+  const float2 t = f2add(x, shifter);                       // round to integer in the mantissa
   const float2 n = f2add(t, make_float2(-12582912.f, -12582912.f));
   const float2 f = f2add(x, make_float2(-n.x, -n.y));
   float2 p = make_float2(0.00960039533674717f, 0.00960039533674717f);
@@ -117,8 +119,9 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x0) {
   p = f2fma(p, f, make_float2(0.24023719131946564f, 0.24023719131946564f));
   p = f2fma(p, f, make_float2(0.6931219696998596f, 0.6931219696998596f));
   p = f2fma(p, f, make_float2(1.0f, 1.0f));
-  return make_float2(__int_as_float(__float_as_int(t.x) * (1 << 23) + __float_as_int(p.x)),
-                     __int_as_float(__float_as_int(t.y) * (1 << 23) + __float_as_int(p.y)));
+  const int ex = __float_as_int(t.x) << 23, ey = __float_as_int(t.y) << 23;
+  return make_float2(x0.x < -125.f ? 0.f : __int_as_float(__float_as_int(p.x) + ex),
+                     x0.y < -125.f ? 0.f : __int_as_float(__float_as_int(p.y) + ey));
 }
 
 template <int D>
@@ -303,7 +306,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const int k0 = j * BN;
       int lim = p.Sk - k0;
       if (p.causal) lim = min(lim, qi + (p.Sk - p.Sq) - k0 + 1);
-      const bool masked = lim < BN;
+      // Warp-uniform: the exp loop below holds warp-collective tcgen05.st.
+      const bool masked = __any_sync(0xffffffffu, lim < BN);
       if (masked) {
 #pragma unroll
         for (int k = 0; k < BN; ++k) x[k] = (k < lim) ? x[k] : -INFINITY;
@@ -345,27 +349,31 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const float mc = (m_used == -INFINITY) ? 0.f : m_used * c;
       const float2 cc = make_float2(c, c), nmc = make_float2(-mc, -mc);
       float2 sum2 = make_float2(0.f, 0.f);
+      // exp, row sum, P store; with POLY, 3 of every 8 pairs run on the FMA pipe.
+      auto exp_store = [&](auto poly_tag) {
+        constexpr bool POLY = decltype(poly_tag)::value;
 #pragma unroll
-      for (int k = 0; k < BN; k += 16) {
-        uint32_t pk[8];
+        for (int k = 0; k < BN; k += 16) {
+          uint32_t pk[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float2 y = f2fma(make_float2(x[k + 2 * t], x[k + 2 * t + 1]), cc, nmc);
-          float2 e;
-          if (t >= 5 && !masked) {
-            e = ex2_poly2(y);                  // 3 of every 8 pairs on the FMA pipe
-          } else {
-            e = make_float2(ex2(y.x), ex2(y.y));
+          for (int t = 0; t < 8; ++t) {
+            const float2 y = f2fma(make_float2(x[k + 2 * t], x[k + 2 * t + 1]), cc, nmc);
+            const float2 e = (POLY && t >= 5) ? ex2_poly2(y) : make_float2(ex2(y.x), ex2(y.y));
+            sum2 = f2add(sum2, e);
+            pk[t] = pack_bf16x2(e.x, e.y);
           }
-          sum2 = f2add(sum2, e);
-          pk[t] = pack_bf16x2(e.x, e.y);
+          tmem_st8(s_addr + k / 2, pk);        // P (bf16 pairs) over S's first 64 columns
+          if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
+          }
         }
-        tmem_st8(s_addr + k / 2, pk);          // P (bf16 pairs) over S's first 64 columns
-        if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
-        }
+      };
+      if (masked) {
+        exp_store(std::false_type{});   // tiles with masked keys: every exp on MUFU
+      } else {
+        exp_store(std::true_type{});
       }
       l += sum2.x + sum2.y;
     }
