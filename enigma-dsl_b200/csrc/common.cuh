@@ -43,6 +43,8 @@ cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x
 // Argument checks of a decode-layer descriptor (ENIGMA_OK or ENIGMA_ERR_BADARG + message).
 int32_t check_decode_desc(const enigma_decode_layer_desc* d);
 
+cudaError_t qwen_decode_f32_launch(const enigma_qwen_decode_f32_desc& q, cudaStream_t s);
+
 // Records a message for enigma_last_error on the calling thread.
 void set_error(const char* fmt, ...);
 

@@ -168,6 +168,22 @@ int32_t enigma_decode_layer_bf16(const enigma_decode_layer_desc* desc, const voi
                        "decode_layer");
 }
 
+int32_t enigma_qwen_decode_f32(const enigma_qwen_decode_f32_desc* d, void* stream) {
+  if (d == nullptr) return bad("qwen decode: desc is NULL");
+  if (d->hidden <= 0 || d->heads_q <= 0 || d->heads_kv <= 0 || d->heads_q % d->heads_kv != 0 ||
+      d->head_dim <= 0 || d->head_dim > 256 || d->head_dim % 2 != 0 || d->intermediate <= 0 ||
+      d->cache_total <= 0)
+    return bad("qwen decode: sizes (head_dim even and <= 256, heads_q multiple of heads_kv)");
+  const void* ptrs[] = {d->x, d->w_norm, d->Wq, d->Wk, d->Wv, d->w_q_norm, d->w_k_norm,
+                        d->cos_pos, d->sin_pos, d->k_cache, d->v_cache, d->Wo, d->w_post,
+                        d->Wg, d->Wu, d->Wd, d->norm_buf, d->q_buf, d->k_buf, d->v_buf,
+                        d->attn_buf, d->mlp_buf, d->post_buf, d->q_rope_buf, d->k_rope_buf,
+                        d->out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned(p, 16)) return bad("qwen decode: NULL or unaligned buffer");
+  return launch_status(enigma::qwen_decode_f32_launch(*d, as_stream(stream)), "qwen_decode_f32");
+}
+
 int32_t enigma_dispatch(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
                         const int64_t* ip, int32_t n_ip, const float* fp, int32_t n_fp,
                         const uint32_t* grid3, const uint32_t* threads3, void* stream) {

@@ -58,6 +58,7 @@ PROTOTYPES = {
                             _c.POINTER(_i64), _f32, _i32, _vp],
     "enigma_decode_workspace_bytes": [_vp, _c.POINTER(_sz)],
     "enigma_decode_layer_bf16": [_vp, _vp, _vp, _vp, _sz, _vp],
+    "enigma_qwen_decode_f32": [_vp, _vp],
     "enigma_decode_layer_bf16_noalloc": [_vp, _vp, _vp, _vp],
     "enigma_dispatch": [_i32, _c.POINTER(_vp), _i32, _c.POINTER(_i64), _i32, _c.POINTER(_f32),
                         _i32, _u32p, _u32p, _vp],

@@ -212,7 +212,7 @@ def _match_gemm(t: _Trace, args: tuple) -> Optional[Binding]:
 
 # ----------------------------------------------------------------------------- decode layer
 def _match_decode(t: _Trace, args: tuple) -> Optional[Binding]:
-    if len(t.b.args) < 20 or not t.has("rsqrt", "exp", "simd_sum"):
+    if len(t.b.args) < 20 or not t.has("rsqrt", "exp", "simd_sum", "scf_for"):
         return None
     from .. import decode_layer
     return decode_layer.bind_from_trace(t)

@@ -18,6 +18,13 @@ from . import _native
 from ._tracing import EnigmaError
 
 
+# Buffer order of the reference's qwen_fused kernel (examples/qwen_megakernel.py:229-240).
+QWEN_BUFFERS = ("x", "w_norm", "Wq", "Wk", "Wv", "w_q_norm", "w_k_norm", "cos_pos", "sin_pos",
+                "k_cache", "v_cache", "Wo", "w_post", "Wg", "Wu", "Wd", "norm_buf", "q_buf",
+                "k_buf", "v_buf", "attn_buf", "mlp_buf", "post_buf", "q_rope_buf", "k_rope_buf",
+                "out")
+
+
 class DecodeDesc(ctypes.Structure):
     """Mirror of enigma_decode_layer_desc (include/enigma_cuda.h)."""
 
@@ -151,10 +158,46 @@ class DecodeLayer:
         return sum(t.numel() * t.element_size() for t in self.w.values())
 
 
+class QwenF32Desc(ctypes.Structure):
+    """Mirror of enigma_qwen_decode_f32_desc (include/enigma_cuda.h)."""
+
+    _fields_ = [(n, ctypes.c_int64) for n in ("hidden", "heads_q", "heads_kv", "head_dim",
+                                              "intermediate", "cache_total")] + \
+               [("eps", ctypes.c_float), ("attn_scale", ctypes.c_float)] + \
+               [(n, ctypes.c_void_p) for n in QWEN_BUFFERS]
+
+
 def bind_from_trace(t):
-    raise EnigmaError("qwen_fused-style fp32 megakernels are not bound yet; use "
-                      "enigma.decode_layer.DecodeLayer for the bf16 decode step")
+    """Bind a qwen_fused-style trace (26 fp32 buffers in the reference's order,
+    examples/qwen_megakernel.py:228-240): eps from the first rsqrt(sum / N + eps)."""
+    from .compiler.recognize import Binding, _rmsnorm_eps
+    if len(t.b.args) != len(QWEN_BUFFERS) or any(a[2] != "float" for a in t.b.args):
+        return None
+    eps, _ = _rmsnorm_eps(t)
+    if eps is None:
+        return None
+    return Binding("decode", "float", {"eps": float(eps)}, layout="qwen_fused_f32")
 
 
 def plan_decode(binding, nbytes):
-    raise EnigmaError("qwen_fused-style fp32 megakernels are not bound yet")
+    """Sizes from the buffers (fp32 elements): x [H], w_q_norm [D], Wq [Hq*D, H],
+    Wk [Hkv*D, H], K cache [Hkv, T, D], Wg [I, H]; attention scale 1/sqrt(D) as in the
+    reference (ATTN_SCALE, qwen_megakernel.py:32)."""
+    from .runtime_dispatch.launch import LaunchPlan
+    n = {name: b // 4 for name, b in zip(QWEN_BUFFERS, nbytes)}
+    H, D = n["x"], n["w_q_norm"]
+    if H <= 0 or D <= 0 or n["Wq"] % (H * D) or n["Wk"] % (H * D):
+        raise RuntimeError("enigma GPU error: qwen decode buffers do not give consistent sizes")
+    hq, hkv = n["Wq"] // (H * D), n["Wk"] // (H * D)
+    total = n["k_cache"] // (hkv * D)
+    inter = n["Wg"] // H
+    eps = float(binding.params["eps"])
+
+    def fn(ptrs, stream):
+        d = QwenF32Desc(hidden=H, heads_q=hq, heads_kv=hkv, head_dim=D, intermediate=inter,
+                        cache_total=total, eps=eps, attn_scale=1.0 / math.sqrt(D))
+        for name, ptr in zip(QWEN_BUFFERS, ptrs):
+            setattr(d, name, ptr)
+        _native.call("enigma_qwen_decode_f32", ctypes.byref(d), stream)
+    return LaunchPlan(f"qwen decode f32 H={H} Hq={hq} Hkv={hkv} D={D} I={inter} T={total}", fn,
+                      (len(QWEN_BUFFERS) - 1,))

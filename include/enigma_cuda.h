@@ -141,6 +141,21 @@ int32_t enigma_decode_workspace_bytes(const enigma_decode_layer_desc* desc, size
 int32_t enigma_decode_layer_bf16(const enigma_decode_layer_desc* desc, const void* x, void* out,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* The reference's own fp32 single-token layer (qwen_fused, examples/qwen_megakernel.py:
+ * 228-269) with its buffer set: weights row-major [out, in] (y = W x); caches
+ * [heads_kv, cache_total, head_dim] already holding the new token's k / v (as the
+ * reference's host prepares them); norm_buf .. k_rope_buf are the reference's scratch
+ * buffers and serve as the workspace.  fp32 throughout; head_dim even and <= 256. */
+typedef struct enigma_qwen_decode_f32_desc {
+  int64_t hidden, heads_q, heads_kv, head_dim, intermediate, cache_total;
+  float eps, attn_scale;
+  const float *x, *w_norm, *Wq, *Wk, *Wv, *w_q_norm, *w_k_norm, *cos_pos, *sin_pos;
+  const float *k_cache, *v_cache, *Wo, *w_post, *Wg, *Wu, *Wd;
+  float *norm_buf, *q_buf, *k_buf, *v_buf, *attn_buf, *mlp_buf, *post_buf, *q_rope_buf,
+      *k_rope_buf, *out;
+} enigma_qwen_decode_f32_desc;
+int32_t enigma_qwen_decode_f32(const enigma_qwen_decode_f32_desc* desc, void* stream);
+
 /* The same decode step without a caller-provided workspace, for callers that cannot
  * allocate device memory on this path: a serving loop that must never enter the
  * allocator, a plugin inside a host runtime that owns all device memory, code where an

@@ -169,3 +169,35 @@ def decode_layer(x, w, k_cache, v_cache, cos, sin, position, heads_q, heads_kv, 
     g, u = gu[:, :inter], gu[:, inter:]
     out = h1 + (g / (1 + np.exp(-g)) * u) @ f["w_down"]
     return out.astype(np.float32), q.astype(np.float32), k.astype(np.float32), v.astype(np.float32)
+
+
+def qwen_decode_f32(x, w_norm, Wq, Wk, Wv, w_q_norm, w_k_norm, cos_p, sin_p, k_cache, v_cache,
+                    Wo, w_post, Wg, Wu, Wd, heads_q, heads_kv, eps):
+    """full_decode_np of examples/qwen_megakernel.py:320-342 for caches that already
+    hold the new k / v (the reference's host pre-fills them, :358-364).  fp64."""
+    f = lambda a: np.asarray(a, np.float64)  # noqa: E731
+    x, Wq, Wk, Wv, Wo, Wg, Wu, Wd = map(f, (x, Wq, Wk, Wv, Wo, Wg, Wu, Wd))
+    D = f(w_q_norm).shape[0]
+    half = D // 2
+
+    def rms(v, w):
+        return v / np.sqrt(np.mean(v * v, axis=-1, keepdims=True) + eps) * f(w)
+
+    def rope(t):
+        lo, hi = t[..., :half], t[..., half:]
+        c, s = f(cos_p), f(sin_p)
+        return np.concatenate([lo * c[:half] - hi * s[:half], hi * c[half:] + lo * s[half:]], -1)
+
+    n1 = rms(x, w_norm)
+    q = rope(rms((Wq @ n1).reshape(heads_q, D), w_q_norm))
+    kc, vc = f(k_cache), f(v_cache)
+    g = heads_q // heads_kv
+    attn = np.empty((heads_q, D))
+    for h in range(heads_q):
+        sc = kc[h // g] @ q[h] / np.sqrt(D)
+        p = np.exp(sc - sc.max())
+        attn[h] = (p / p.sum()) @ vc[h // g]
+    o = Wo @ attn.ravel() + x
+    post = rms(o, w_post)
+    gate, up = Wg @ post, Wu @ post
+    return (Wd @ (gate / (1 + np.exp(-gate)) * up) + o).astype(np.float32)

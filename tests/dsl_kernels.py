@@ -219,3 +219,121 @@ def make_async_gemm(m, n, k, tm=32, tn=32, tk=16):
         C[(bx * tm) * nc + by * tn + enigma.thread_position_in_threadgroup()] = acc[0, 0]
 
     return gemm_async
+
+
+# ---------------------------------------------------------------- Qwen single-layer decode
+# examples/qwen_megakernel.py:41-269: one threadgroup, phases separated by device barriers.
+def make_qwen(H, INTER, QH, KVH, CACHE_TOTAL, eps=1e-6, TG=256):
+    HD = H // QH
+    G = QH // KVH
+    scale = 1.0 / float(HD) ** 0.5
+
+    def u(v):
+        return enigma.metal_cast(v, "uint")
+
+    def rmsnorm(X, W, Y, dim, tid):
+        lane = enigma.thread_index_in_simdgroup()
+        sg = enigma.simdgroup_index_in_threadgroup()
+        z = enigma.metal_cast(0, "float")
+        with enigma.for_range(0, dim // TG, init=[z]) as (j, c):
+            v = X[tid + u(j) * u(TG)]
+            c[0] = c[0] + v * v
+        part = enigma.simd_sum(c[0])
+        scratch = enigma.threadgroup_alloc("float", 32)
+        enigma.store_if(scratch, sg, part, enigma.cmp_eq(lane, 0))
+        enigma.barrier()
+        tot = enigma.simd_sum(enigma.load_if(scratch, lane,
+                                             enigma.cmp_ult(lane, enigma.simdgroups_per_threadgroup()),
+                                             default=0.0))
+        r = enigma.rsqrt(tot / float(dim) + eps)
+        with enigma.for_range(0, dim // TG) as j:
+            idx = tid + u(j) * u(TG)
+            Y[idx] = (X[idx] * r) * W[idx]
+
+    def matvec(X, W, Out, rows, cols, tid, res=None, Wu=None):
+        with enigma.for_range(0, (rows + TG - 1) // TG) as ch:
+            row = tid + u(ch) * u(TG)
+            with enigma.if_(enigma.cmp_ult(row, u(rows))):
+                z = enigma.metal_cast(0, "float")
+                init = [z, z] if Wu is not None else [z]
+                with enigma.for_range(0, cols, init=init) as (i, c):
+                    xv = X[u(i)]
+                    c[0] = enigma.fma(W[row * u(cols) + u(i)], xv, c[0])
+                    if Wu is not None:
+                        c[1] = enigma.fma(Wu[row * u(cols) + u(i)], xv, c[1])
+                if Wu is not None:
+                    one = enigma.metal_cast(1, "float")
+                    Out[row] = (c[0] * (one / (one + enigma.exp(-c[0])))) * c[1]
+                else:
+                    Out[row] = c[0] + res[row] if res is not None else c[0]
+
+    def head_norm_rope(src, w, cs, sn, dst, nh, tid):
+        with enigma.if_(enigma.cmp_ult(tid, u(nh))):
+            base = tid * u(HD)
+            z = enigma.metal_cast(0, "float")
+            with enigma.for_range(0, HD, init=[z]) as (k, c):
+                v = src[base + u(k)]
+                c[0] = c[0] + v * v
+            sc = enigma.rsqrt(c[0] / float(HD) + eps)
+            with enigma.for_range(0, HD) as k:
+                dst[base + u(k)] = src[base + u(k)] * sc * w[u(k)]
+            with enigma.for_range(0, HD // 2) as k:
+                lo_i, hi_i = base + u(k), base + u(k) + u(HD // 2)
+                lo, hi = dst[lo_i], dst[hi_i]
+                dst[lo_i] = lo * cs[u(k)] - hi * sn[u(k)]
+                dst[hi_i] = hi * cs[u(k) + u(HD // 2)] + lo * sn[u(k) + u(HD // 2)]
+
+    def sdpa(Q, K, V, O, tid):
+        with enigma.if_(enigma.cmp_ult(tid, u(QH))):
+            kvh = tid / u(G)
+            neg, z = enigma.metal_cast(-1e30, "float"), enigma.metal_cast(0, "float")
+            with enigma.for_range(0, CACHE_TOTAL, init=[neg, z]) as (pos, c):
+                with enigma.for_range(0, HD, init=[z]) as (d, dc):
+                    dc[0] = enigma.fma(Q[tid * u(HD) + u(d)],
+                                       K[kvh * u(CACHE_TOTAL * HD) + u(pos) * u(HD) + u(d)], dc[0])
+                s = dc[0] * scale
+                mn = enigma.fmax(c[0], s)
+                c[1] = c[1] * enigma.exp(c[0] - mn) + enigma.exp(s - mn)
+                c[0] = mn
+            m_fin = c[0]
+            inv_l = enigma.metal_cast(1, "float") / c[1]
+            with enigma.for_range(0, HD) as d:
+                with enigma.for_range(0, CACHE_TOTAL, init=[z]) as (pos, vc):
+                    with enigma.for_range(0, HD, init=[z]) as (d2, dc2):
+                        dc2[0] = enigma.fma(Q[tid * u(HD) + u(d2)],
+                                            K[kvh * u(CACHE_TOTAL * HD) + u(pos) * u(HD) + u(d2)],
+                                            dc2[0])
+                    p = enigma.exp(dc2[0] * scale - m_fin) * inv_l
+                    vc[0] = vc[0] + p * V[kvh * u(CACHE_TOTAL * HD) + u(pos) * u(HD) + u(d)]
+                O[tid * u(HD) + u(d)] = vc[0]
+
+    @enigma.kernel
+    def qwen_fused(X: enigma.f32, w_norm: enigma.f32, Wq: enigma.f32, Wk: enigma.f32,
+                   Wv: enigma.f32, w_q_norm: enigma.f32, w_k_norm: enigma.f32,
+                   cos_pos: enigma.f32, sin_pos: enigma.f32, K_cache: enigma.f32,
+                   V_cache: enigma.f32, Wo: enigma.f32, w_post: enigma.f32, Wg: enigma.f32,
+                   Wu: enigma.f32, Wd: enigma.f32, norm_buf: enigma.f32, q_buf: enigma.f32,
+                   k_buf: enigma.f32, v_buf: enigma.f32, attn_buf: enigma.f32,
+                   mlp_buf: enigma.f32, post_buf: enigma.f32, q_rope_buf: enigma.f32,
+                   k_rope_buf: enigma.f32, Out: enigma.f32):
+        tid = enigma.thread_position_in_threadgroup()
+        rmsnorm(X, w_norm, norm_buf, H, tid)
+        enigma.barrier("mem_device_and_threadgroup")
+        matvec(norm_buf, Wq, q_buf, QH * HD, H, tid)
+        matvec(norm_buf, Wk, k_buf, KVH * HD, H, tid)
+        matvec(norm_buf, Wv, v_buf, KVH * HD, H, tid)
+        enigma.barrier("mem_device_and_threadgroup")
+        head_norm_rope(q_buf, w_q_norm, cos_pos, sin_pos, q_rope_buf, QH, tid)
+        head_norm_rope(k_buf, w_k_norm, cos_pos, sin_pos, k_rope_buf, KVH, tid)
+        enigma.barrier("mem_device_and_threadgroup")
+        sdpa(q_rope_buf, K_cache, V_cache, attn_buf, tid)
+        enigma.barrier("mem_device_and_threadgroup")
+        matvec(attn_buf, Wo, norm_buf, H, QH * HD, tid, res=X)
+        enigma.barrier("mem_device_and_threadgroup")
+        rmsnorm(norm_buf, w_post, post_buf, H, tid)
+        enigma.barrier("mem_device_and_threadgroup")
+        matvec(post_buf, Wg, mlp_buf, INTER, H, tid, Wu=Wu)
+        enigma.barrier("mem_device_and_threadgroup")
+        matvec(mlp_buf, Wd, Out, H, INTER, tid, res=norm_buf)
+
+    return qwen_fused

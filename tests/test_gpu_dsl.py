@@ -125,3 +125,35 @@ def test_bind_count_error(rt):
 def test_device_capabilities(rt):
     caps = rt.device_capabilities()
     assert caps.gpu_family == "sm_100" and caps.sm_count >= 100 and caps.simdgroup_size == 32
+
+
+@pytest.mark.parametrize("H,INTER,QH,KVH,CT", [(1024, 3072, 16, 8, 33), (256, 512, 4, 2, 9)])
+def test_qwen_fused_reference_shape(rt, H, INTER, QH, KVH, CT):
+    """examples/qwen_megakernel.py: fp32, one token, caches pre-filled; its bar is 1e-3."""
+    HD = H // QH
+    ck = enigma.compile(K.make_qwen(H, INTER, QH, KVH, CT))
+    rng = np.random.default_rng(0)
+    f32 = lambda a: np.asarray(a, np.float32)  # noqa: E731
+    x = f32(rng.standard_normal(H) * 0.1)
+    w_in, w_post = f32(rng.standard_normal(H) * 0.1 + 1), f32(rng.standard_normal(H) * 0.1 + 1)
+    wqn, wkn = f32(rng.standard_normal(HD) * 0.1 + 1), f32(rng.standard_normal(HD) * 0.1 + 1)
+    Wq = f32(rng.standard_normal((QH * HD, H)) / np.sqrt(H))
+    Wk = f32(rng.standard_normal((KVH * HD, H)) / np.sqrt(H))
+    Wv = f32(rng.standard_normal((KVH * HD, H)) / np.sqrt(H))
+    Wo = f32(rng.standard_normal((H, QH * HD)) / np.sqrt(QH * HD))
+    Wg = f32(rng.standard_normal((INTER, H)) / np.sqrt(H))
+    Wu = f32(rng.standard_normal((INTER, H)) / np.sqrt(H))
+    Wd = f32(rng.standard_normal((H, INTER)) / np.sqrt(INTER))
+    ang = np.arange(HD, dtype=np.float32) / HD * (np.pi / 2)
+    cs, sn = f32(np.cos(ang)), f32(np.sin(ang))
+    kc = f32(rng.standard_normal((KVH, CT, HD)) * 0.1)
+    vc = f32(rng.standard_normal((KVH, CT, HD)) * 0.1)
+    z = lambda n: np.zeros(n, np.float32)  # noqa: E731
+    ins = [x, w_in, Wq.ravel(), Wk.ravel(), Wv.ravel(), wqn, wkn, cs, sn, kc.ravel(), vc.ravel(),
+           Wo.ravel(), w_post, Wg.ravel(), Wu.ravel(), Wd.ravel(), z(H), z(QH * HD), z(KVH * HD),
+           z(KVH * HD), z(QH * HD), z(INTER), z(H), z(QH * HD), z(KVH * HD)]
+    raw = rt.execute(ck, ins, H * 4, grid=(256, 1, 1), threads=(256, 1, 1))
+    out = np.frombuffer(raw, np.float32)
+    ref = orc.qwen_decode_f32(x, w_in, Wq, Wk, Wv, wqn, wkn, cs, sn, kc, vc, Wo, w_post, Wg, Wu,
+                              Wd, QH, KVH, 1e-6)
+    assert np.max(np.abs(out - ref)) < 1e-4, np.max(np.abs(out - ref))

@@ -67,3 +67,10 @@ def test_launch_outside_compile_raises():
 def test_tracing_records_loops_and_carries():
     ck = enigma.compile(K.make_fa(64))
     assert "scf_for" in ck.metal_source and "exp" in ck.metal_source
+
+
+def test_qwen_fused_binding():
+    ck = enigma.compile(K.make_qwen(256, 512, 4, 2, 9))
+    b = ck.cuda_kernel
+    assert (b.op, b.layout) == ("decode", "qwen_fused_f32") and b.params["eps"] == pytest.approx(1e-6)
+    assert ck.num_params == 26
