@@ -18,7 +18,7 @@
 //               the main loop of tile i+1.
 // Tiles are walked in groups of 8 M-blocks so that consecutive CTAs share B
 // columns in L2.  Ragged M/N/K edges are zero-filled by TMA and masked on store.
-// No TMA load uses cluster multicast.
+// Each CTA issues its own TMA loads.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

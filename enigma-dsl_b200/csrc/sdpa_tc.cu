@@ -11,7 +11,7 @@
 //
 //   warp 0      TMA: Q0, Q1 once; K and V tiles into 2-stage rings (128B swizzle,
 //               3-D tensor maps [D, S, B*H]: ragged S zero-fills and never reads
-//               the next head).  No multicast.
+//               the next head).  Each CTA loads its own tiles.
 //   warp 1      one lane issues tcgen05.mma (fp32 accumulators in TMEM):
 //                 S_i = Q_i K_j^T   (SS, M128 N128)          i = 0, 1
 //                 O_i += P_i V_j    (TS: P read from TMEM over S_i's columns)

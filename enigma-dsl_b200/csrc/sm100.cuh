@@ -4,7 +4,7 @@
 //
 // Written from the public PTX ISA description (mbarrier, cp.async.bulk.tensor,
 // tcgen05.{alloc,dealloc,mma,commit,ld,wait,fence}).  No TMA load here ever
-// uses .multicast::cluster: every CTA fetches its own tiles.
+// is shared across a cluster: every CTA fetches its own tiles.
 //
 // Every wait on an mbarrier is bounded: after kSpinLimit polls the waiter
 // records an error code in the kernel's status word and gives up, so a bug
