@@ -22,6 +22,9 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace {
@@ -212,6 +215,191 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
   }
 }
 
+// ============================================================================ 2-SM variant
+// A cluster of two CTAs (a "CTA pair" on neighbouring SMs) owns one 256x256 tile:
+// tcgen05.mma.cta_group::2 (M = 256, N = 256) is issued by the pair's leader (rank 0)
+// and reads A rows 0-127 / B columns 0-127 from the leader's shared memory and A rows
+// 128-255 / B columns 128-255 from the peer's; each CTA's TMEM holds its own 128 rows
+// of the 256-wide accumulator.  Per SM this moves 32 KB of operands per 64-deep K step
+// instead of 48 KB for the same FLOPs, easing shared-memory bandwidth.
+//   both CTAs, warp 0   TMA of the CTA's A half and B half; completion bytes counted on
+//                       the leader's full[stage] barrier (cta_group::2 form of the load)
+//   leader, warp 1      MMA issue; releases a stage / publishes an accumulator by
+//                       committing to the barrier in both CTAs
+//   both CTAs, warps 2-5 epilogue of the CTA's 128 rows; arrive on the leader's
+//                       acc_empty (256 arrivals per accumulator)
+constexpr int P_BM = 256;                              // tile rows per pair
+constexpr int P_BN = 256;                              // tile columns per pair
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = (P_BM / 2) * BK * 2;         // 16 KB: this CTA's 128 rows
+constexpr int P_B_BYTES = BK * (P_BN / 2) * 2;         // 16 KB: this CTA's 128 columns
+constexpr int P_STAGE = P_A_BYTES + P_B_BYTES;
+constexpr int P_SMEM = P_STAGES * P_STAGE + 1024 + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, __nv_bfloat16* __restrict__ C,
+                      int M, int N, int K, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + P_STAGES * P_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* acc_full = empty + P_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * EPI_THREADS);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated, before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const TileSched sched{(M + P_BM - 1) / P_BM, (N + P_BN - 1) / P_BN};
+  const int num_tiles = sched.num_m * sched.num_n;
+  const int num_kb = (K + BK - 1) / BK;
+  const int pair_id = int(blockIdx.x) >> 1, num_pairs = int(gridDim.x) >> 1;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (elect_one()) {
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+        int mb, nb;
+        sched.coords(t, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, status)) { ok = false; break; }
+          const uint32_t fb = full_leader0 + stage * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE);
+          tma_load_2d_pair(sA + stage * P_A_BYTES, &tmA, fb, kb * BK, mb * P_BM + int(rank) * 128);
+          uint8_t* b = sB + stage * P_B_BYTES;
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            tma_load_2d_pair(b + j * B_BOX_BYTES, &tmB, fb, nb * P_BN + int(rank) * 128 + j * 64,
+                             kb * BK);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only)
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, P_BN, /*a_mn=*/false, /*b_mn=*/true);
+      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+      const uint32_t empty0_self = smem_u32(&empty[0]), empty0_peer = mapa_shared(empty0_self, peer);
+      const uint32_t accf0_self = smem_u32(&acc_full[0]), accf0_peer = mapa_shared(accf0_self, peer);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * P_BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(a0 + stage * P_A_BYTES, 16, 1024);
+          const uint64_t db = smem_desc_sw128(b0 + stage * P_B_BYTES, B_BOX_BYTES, 1024);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_bf16_ss_pair(d, da + uint64_t((kk * 32) >> 4), db + uint64_t((kk * 2048) >> 4),
+                             idesc, (kb | kk) != 0 ? 1u : 0u);
+          mma_commit_pair(empty0_self + stage * 8);
+          mma_commit_pair(empty0_peer + stage * 8);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit_pair(accf0_self + acc * 8);
+        mma_commit_pair(accf0_peer + acc * 8);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of each 256-row tile
+    const int quarter = warp & 3;
+    const int row_in_tile = int(rank) * 128 + quarter * 32 + lane;
+    const uint32_t acce0_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair_id; t < num_tiles; t += num_pairs) {
+      int mb, nb;
+      sched.coords(t, mb, nb);
+      if (!mbar_wait(&acc_full[acc], acc_phase, status)) break;
+      tc_fence_after();
+      const int row = mb * P_BM + row_in_tile;
+      const int col0 = nb * P_BN;
+      __nv_bfloat16* crow = C + int64_t(row) * N;
+      const uint32_t taddr = tmem_base + acc * P_BN + (uint32_t(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < P_BN; c += 32) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(taddr + c, r0);
+        tmem_ld16(taddr + c + 16, r1);
+        tmem_wait_ld();
+        if (row < M && col0 + c < N) {
+          uint32_t p[16];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            p[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+            p[8 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+          }
+          __nv_bfloat16* dst = crow + col0 + c;
+          if (col0 + c + 32 <= N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+          } else {
+            const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(p);
+            for (int i = 0; i < 32 && col0 + c + i < N; ++i) dst[i] = pb[i];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acce0_leader + acc * 8);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // CUDA-core GEMM for shapes the TMA path cannot describe (row pitch not a
 // multiple of 16 bytes, e.g. K = 4).  16x16 output tile per CTA, fp32 accumulate.
 template <typename T>
@@ -284,6 +472,17 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
     cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
+    if (M >= 256 && N >= 256 && !(getenv("ENIGMA_GEMM_1SM") && getenv("ENIGMA_GEMM_1SM")[0] == '1')) {
+      // CTA-pair kernel: B boxes of the pair's two N halves, A boxes of 128 rows.
+      e = cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               P_SMEM);
+      if (e != cudaSuccess) return e;
+      const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
+      const int pairs = int(std::min<int64_t>(ptiles, sm_count() / 2));
+      gemm_bf16_pair_kernel<<<2 * pairs, THREADS, P_SMEM, s>>>(
+          ta, tb, static_cast<__nv_bfloat16*>(C), int(M), int(N), int(K), device_status());
+      return cudaGetLastError();
+    }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = int(tiles < sm_count() ? tiles : sm_count());
     gemm_bf16_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(
