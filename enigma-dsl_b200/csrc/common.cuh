@@ -45,6 +45,9 @@ int32_t check_decode_desc(const enigma_decode_layer_desc* d);
 
 cudaError_t qwen_decode_f32_launch(const enigma_qwen_decode_f32_desc& q, cudaStream_t s);
 
+cudaError_t elementwise_launch(int op, int dtype, const void* a, const void* b, void* c, int64_t n,
+                               cudaStream_t s);
+
 // Records a message for enigma_last_error on the calling thread.
 void set_error(const char* fmt, ...);
 

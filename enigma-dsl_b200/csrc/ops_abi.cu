@@ -41,6 +41,19 @@ int32_t enigma_rmsnorm(int32_t dtype, const void* x, const void* w, void* y, int
       enigma::rmsnorm_launch(dtype, x, w, y, rows, hidden, eps, as_stream(stream)), "rmsnorm");
 }
 
+int32_t enigma_elementwise(int32_t op, int32_t dtype, const void* A, const void* B, void* C,
+                           int64_t n, void* stream) {
+  if (op < 0 || op > 4) return bad("elementwise: op must be 0..4");
+  if (dtype != ENIGMA_DTYPE_F32 && dtype != ENIGMA_DTYPE_BF16) return bad("elementwise: dtype");
+  if (n < 0) return bad("elementwise: n < 0");
+  if (n == 0) return ENIGMA_OK;
+  if (A == nullptr || B == nullptr || C == nullptr) return bad("elementwise: NULL buffer");
+  if (!aligned(A, 16) || !aligned(B, 16) || !aligned(C, 16))
+    return bad("elementwise: buffers must be 16-byte aligned");
+  return launch_status(enigma::elementwise_launch(op, dtype, A, B, C, n, as_stream(stream)),
+                       "elementwise");
+}
+
 int32_t enigma_gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                          void* stream) {
   if (M < 0 || N < 0 || K < 0) return bad("gemm: negative size");

@@ -52,6 +52,7 @@ PROTOTYPES = {
     "enigma_rmsnorm": [_i32, _vp, _vp, _vp, _i64, _i64, _f32, _vp],
     "enigma_gemm_bf16": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "enigma_sdpa_bf16": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp],
+    "enigma_elementwise": [_i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "enigma_gemm_f32": [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp],
     "enigma_sdpa_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp],
     "enigma_sdpa_strided": [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -28,6 +28,8 @@ Fingerprints (op kinds present in the trace, buffer signature):
              stages tiles for: the shipped example never multiplies)
   decode     the Qwen single-layer decode megakernel (26 buffers)
              -- examples/qwen_megakernel.py:228-269
+  elementwise  C = A op B with exactly one value op on two loads, per TV value or per
+             thread -- examples/vector_add_tv.py:13-55, examples/vector_add.py
 """
 from __future__ import annotations
 
@@ -218,7 +220,44 @@ def _match_decode(t: _Trace, args: tuple) -> Optional[Binding]:
     return decode_layer.bind_from_trace(t)
 
 
-_MATCHERS = (_match_decode, _match_rmsnorm, _match_sdpa, _match_gemm)
+# ----------------------------------------------------------------------------- elementwise
+_EW_OPS = {"add": 0, "sub": 1, "mul": 2, "fmax": 3, "fmin": 4}
+_EW_ALLOWED = {"tv_load", "tv_store", "load", "store", "const", "cast", "add", "sub", "mul",
+               "div", "mod", "thread_position_in_grid", "thread_position_in_threadgroup",
+               "threadgroup_position_in_grid", "threads_per_threadgroup"}
+
+
+def _match_elementwise(t: _Trace, args: tuple) -> Optional[Binding]:
+    """C = A op B, one element per thread (examples/vector_add.py) or per TV value
+    (examples/vector_add_tv.py:13-55): exactly one value op combining the two loads."""
+    if len(t.b.args) != 3:
+        return None
+    dtypes = {a[2] for a in t.b.args}
+    if len(dtypes) != 1 or not dtypes <= {"float", "bfloat"}:
+        return None
+    kinds = set(t.kinds)
+    tv = {"tv_add": 0, "tv_sub": 1, "tv_mul": 2}
+    if kinds & {"tv_load"}:
+        ops = [k for k in kinds if k in tv]
+        if len(ops) != 1 or t.kinds[ops[0]] != 1 or t.kinds["tv_load"] != 2 or \
+                t.kinds["tv_store"] != 1 or kinds - _EW_ALLOWED - set(tv):
+            return None
+        runs = [c for op in t.ops if op.op == "tv_load" for _, c in op.attrs["groups"]]
+        return Binding("elementwise", dtypes.pop(), {"op": tv[ops[0]], "vector_run": max(runs)},
+                       layout="tv")
+    if t.kinds["load"] != 2 or t.kinds["store"] != 1 or kinds - _EW_ALLOWED - {"fmax", "fmin"}:
+        return None
+    store = next(op for op in t.ops if op.op == "store")
+    val = t.def_of(store.operands[1])
+    if val is None or val.op not in _EW_OPS:
+        return None
+    srcs = [t.def_of(o) for o in val.operands]
+    if not all(s is not None and s.op == "load" for s in srcs):
+        return None
+    return Binding("elementwise", dtypes.pop(), {"op": _EW_OPS[val.op]}, layout="naive")
+
+
+_MATCHERS = (_match_decode, _match_rmsnorm, _match_sdpa, _match_gemm, _match_elementwise)
 
 
 def recognize(builder: KernelBuilder, args: tuple = ()) -> Binding:

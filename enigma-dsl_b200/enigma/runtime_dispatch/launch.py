@@ -46,6 +46,8 @@ def plan(binding, nbytes: List[int], grid: Tuple[int, ...], threads: Tuple[int, 
         return _plan_gemm(binding, nbytes)
     if op == "sdpa":
         return _plan_sdpa(binding, nbytes, grid, threads)
+    if op == "elementwise":
+        return _plan_elementwise(binding, nbytes)
     if op == "decode":
         from ..decode_layer import plan_decode
         return plan_decode(binding, nbytes)
@@ -120,3 +122,15 @@ def _plan_sdpa(b, nbytes, grid, threads):
         _native.call(name, p[0], p[1], p[2], p[3], 1, 1, 1, sq, sk, d, ctypes.c_float(scale),
                      causal, stream)
     return LaunchPlan(f"sdpa rows Sq={sq} Sk={sk} D={d} scale={scale}", fn, (3,))
+
+
+def _plan_elementwise(b, nbytes):
+    _need(len(nbytes) == 3, f"elementwise binds 3 buffers (A, B, C), got {len(nbytes)}")
+    es, dt = _ES[b.dtype], _DT[b.dtype]
+    n = _div(nbytes[0], es, "elementwise A")
+    _need(nbytes[1] >= n * es and nbytes[2] >= n * es, "elementwise: B / C smaller than A")
+    opc = int(b.params["op"])
+
+    def fn(p, stream):
+        _native.call("enigma_elementwise", opc, dt, p[0], p[1], p[2], n, stream)
+    return LaunchPlan(f"elementwise op={opc} n={n}", fn, (2,))

@@ -98,6 +98,13 @@ int32_t enigma_sdpa_bf16(const void* Q, const void* K, const void* V, void* O, i
                          int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
                          int64_t head_dim, float scale, int32_t causal, void* stream);
 
+/* C[i] = A[i] op B[i] for i < n; op 0 add, 1 sub, 2 mul, 3 max, 4 min; fp32 or bf16.
+ * Replaces the dispatch of add_kernel (examples/vector_add_tv.py:13-55) and the
+ * one-thread-per-element kernels of examples/vector_add.py.  Buffers 16-byte aligned
+ * for the vector path (any alignment of the element size works, slower). */
+int32_t enigma_elementwise(int32_t op, int32_t dtype, const void* A, const void* B, void* C,
+                           int64_t n, void* stream);
+
 /* fp32 reference-shape variants on CUDA cores (exact fp32 FMA accumulation):
  * C[M,N] (+)= A[M,K] * B[K,N] — replaces matmul_k4 / gemm_k4
  * (tests/metal/test_gemm_matmul_runtime.py:20-60); `accumulate` != 0 adds into C. */

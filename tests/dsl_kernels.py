@@ -337,3 +337,34 @@ def make_qwen(H, INTER, QH, KVH, CACHE_TOTAL, eps=1e-6, TG=256):
         matvec(mlp_buf, Wd, Out, H, INTER, tid, res=norm_buf)
 
     return qwen_fused
+
+
+# ---------------------------------------------------------------- TV elementwise add
+# examples/vector_add_tv.py:13-55: (4,64) threads x (4,4) values per 64x... tile.
+def make_tv_add(M, N, dtype="float"):
+    @enigma.kernel
+    def add_kernel(gA, gB, gC, tv_layout, tiler):
+        tidx, _, _ = enigma.arch.thread_idx()
+        bidx, _, _ = enigma.arch.block_idx()
+        frag = [tensor_composition(g[((None, None), bidx)], tv_layout, tiler)[(tidx, None)]
+                for g in (gA, gB, gC)]
+        frag[2].store(frag[0].load() + frag[1].load())
+
+    @enigma.jit
+    def elementwise_add(mA, mB, mC):
+        tiler, tv = enigma.make_layout_tv(enigma.make_ordered_layout((4, 64), order=(1, 0)),
+                                          enigma.make_ordered_layout((4, 4), order=(1, 0)))
+        gs = [tensor_zipped_divide(m, tiler) for m in (mA, mB, mC)]
+        blocks, threads = enigma.size(gs[0], mode=[1]), enigma.size(tv, mode=[0])
+        add_kernel(*gs, tv, tiler).launch(grid=(blocks * threads, 1, 1), block=(threads, 1, 1))
+
+    args = tuple(Tensor(n, i, dtype, enigma.Layout((M, N), (N, 1))) for i, n in enumerate("ABC"))
+    return elementwise_add, args
+
+
+def make_naive_binary(op):
+    @enigma.kernel
+    def binary(A: enigma.f32, B: enigma.f32, C: enigma.f32):
+        i = enigma.thread_position_in_grid
+        C[i] = op(A[i], B[i])
+    return binary

@@ -157,3 +157,24 @@ def test_qwen_fused_reference_shape(rt, H, INTER, QH, KVH, CT):
     ref = orc.qwen_decode_f32(x, w_in, Wq, Wk, Wv, wqn, wkn, cs, sn, kc, vc, Wo, w_post, Wg, Wu,
                               Wd, QH, KVH, 1e-6)
     assert np.max(np.abs(out - ref)) < 1e-4, np.max(np.abs(out - ref))
+
+
+def test_tv_add_reference_shape(rt):
+    """examples/vector_add_tv.py: 256 x 512 fp32, rtol 1e-5."""
+    jit, args = K.make_tv_add(256, 512)
+    ck = enigma.compile(jit, *args)
+    rng = np.random.default_rng(0)
+    a, b = (rng.standard_normal((256, 512)).astype(np.float32) for _ in range(2))
+    raw = rt.execute(ck, [a.ravel(), b.ravel()], a.nbytes, grid=ck.grid, threads=ck.block)
+    np.testing.assert_allclose(np.frombuffer(raw, np.float32).reshape(256, 512), a + b,
+                               rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("n", [4, 256, 1024, 65536, 1001])
+def test_naive_add(rt, n):
+    """tests/metal/test_vector_add_runtime.py sizes, rtol 1e-5 (1001: ragged tail)."""
+    ck = enigma.compile(K.make_naive_binary(lambda a, b: a + b))
+    rng = np.random.default_rng(n)
+    a, b = (rng.standard_normal(n).astype(np.float32) for _ in range(2))
+    raw = rt.execute(ck, [a, b], a.nbytes, grid=(n, 1, 1), threads=(min(n, 256), 1, 1))
+    np.testing.assert_allclose(np.frombuffer(raw, np.float32), a + b, rtol=1e-5)

@@ -50,12 +50,12 @@ def test_async_gemm_binding():
 
 def test_unrecognised_kernel_raises():
     @enigma.kernel
-    def add(A: enigma.f32, B: enigma.f32, C: enigma.f32):
+    def wave(A: enigma.f32, B: enigma.f32, C: enigma.f32):
         i = enigma.thread_position_in_grid
-        C[i] = A[i] + B[i]
+        C[i] = enigma.sin(A[i]) * B[i]
 
     with pytest.raises(enigma.EnigmaError, match="no sm_100a implementation"):
-        enigma.compile(add)
+        enigma.compile(wave)
 
 
 def test_launch_outside_compile_raises():
@@ -74,3 +74,16 @@ def test_qwen_fused_binding():
     b = ck.cuda_kernel
     assert (b.op, b.layout) == ("decode", "qwen_fused_f32") and b.params["eps"] == pytest.approx(1e-6)
     assert ck.num_params == 26
+
+
+def test_tv_add_binding():
+    jit, args = K.make_tv_add(256, 512)
+    b = enigma.compile(jit, *args).cuda_kernel
+    assert (b.op, b.layout, b.params["op"]) == ("elementwise", "tv", 0)
+
+
+@pytest.mark.parametrize("fn,code", [(lambda a, b: a + b, 0), (lambda a, b: a * b, 2),
+                                     (lambda a, b: enigma.fmax(a, b), 3)])
+def test_naive_binary_binding(fn, code):
+    b = enigma.compile(K.make_naive_binary(fn)).cuda_kernel
+    assert (b.op, b.layout, b.params["op"]) == ("elementwise", "naive", code)
