@@ -449,13 +449,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [D, S, BH] bf16 view of a contiguous [BH, S, D] tensor; 64 x 128 x 1 boxes.
-bool make_map_3d(CUtensorMap* m, const void* base, int64_t D, int64_t S, int64_t BH) {
+// [D, S, BH] bf16 view of a contiguous [BH, S, D] tensor; 64 x box_rows x 1 boxes.
+bool make_map_3d(CUtensorMap* m, const void* base, int64_t D, int64_t S, int64_t BH,
+                 uint32_t box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(S), cuuint64_t(BH)};
   cuuint64_t strides[2] = {cuuint64_t(D * 2), cuuint64_t(S * D * 2)};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -467,8 +468,10 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
                       int64_t Hkv, int64_t Sq, int64_t Sk, float scale, bool causal,
                       cudaStream_t s) {
   CUtensorMap mq, mk, mv;
-  if (!make_map_3d(&mq, Q, D, Sq, B * Hq) || !make_map_3d(&mk, K, D, Sk, B * Hkv) ||
-      !make_map_3d(&mv, V, D, Sk, B * Hkv))
+  // Q boxes are BM rows (one Q tile), K / V boxes BN rows (one KV tile): the byte counts
+  // the producer expects (Q_BYTES, KV_BYTES) are exactly what these boxes deliver.
+  if (!make_map_3d(&mq, Q, D, Sq, B * Hq, BM) || !make_map_3d(&mk, K, D, Sk, B * Hkv, BN) ||
+      !make_map_3d(&mv, V, D, Sk, B * Hkv, BN))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(sdpa_fwd_tc_kernel<D>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM);
