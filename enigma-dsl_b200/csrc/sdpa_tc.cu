@@ -60,7 +60,7 @@ struct Cfg {
   static constexpr int Q_BYTES = BM * D * 2;     // one Q tile
   static constexpr int KV_BYTES = BN * D * 2;    // one K tile == one V tile
   static constexpr int KATOMS = D / 64;          // 128-byte swizzle atoms along D
-  static constexpr int SMEM = 2 * Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 256;
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 512;
   static constexpr uint32_t TMEM_COLS = 512;     // S0a S0b S1a S1b (64 each) | O0 | O1
   static constexpr uint32_t O_COL = 4 * BN;
 };
@@ -141,8 +141,11 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint64_t* v_full = k_empty + KV_STAGES;
   uint64_t* v_empty = v_full + KV_STAGES;
   uint64_t* s_full = v_empty + KV_STAGES;    // [2 tiles][2 S buffers]
-  uint64_t* p_full = s_full + 4;             // [2 tiles][2 halves of the keys]
-  uint64_t* pv_done = p_full + 4;            // [2 tiles]: one completion per PV
+  // [2 tiles][2 S buffers][2 halves of the keys].  One set per S buffer: the softmax may
+  // run a step ahead of the PV that consumes its previous P, so a single per-tile barrier
+  // could complete two phases before the MMA thread waits on the first.
+  uint64_t* p_full = s_full + 4;
+  uint64_t* pv_done = p_full + 8;            // [2 tiles]: one completion per PV
   uint64_t* o_done = pv_done + 2;            // [2 tiles]: after the last PV
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
@@ -177,10 +180,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-    }
+    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&p_full[i], 128);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&pv_done[i], 1);
       mbar_init(&o_done[i], 1);
@@ -251,7 +252,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const uint64_t dv = smem_desc_sw128(v_addr + s * C::KV_BYTES, BN * 128, 1024);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          if (!mbar_wait(&p_full[2 * i + half], j & 1, p.status)) return false;
+          if (!mbar_wait(&p_full[4 * i + 2 * (j & 1) + half], (j >> 1) & 1, p.status)) return false;
           tc_fence_after();
 #pragma unroll
           for (int kk = half * (BN / 32); kk < (half + 1) * (BN / 32); ++kk)
@@ -383,7 +384,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
+            mbar_arrive(&p_full[4 * ti + 2 * buf + (k == BN - 16 ? 1 : 0)]);
           }
         }
       };
