@@ -7,27 +7,28 @@
 // examples/showcase_attention.py:31-91, check at :150-153).
 //
 // One CTA owns two 128-row Q tiles (Q0, Q1) of one (batch, head) and streams
-// 64-key K/V tiles past both:
+// 128-key K/V tiles past both:
 //
-//   warp 0      TMA: Q0, Q1 once; K and V tiles into 4-stage rings (128B swizzle,
+//   warp 0      TMA: Q0, Q1 once; K and V tiles into 2-stage rings (128B swizzle,
 //               3-D tensor maps [D, S, B*H]: ragged S zero-fills and never reads
 //               the next head).  Each CTA loads its own tiles.
 //   warp 1      one lane issues tcgen05.mma (fp32 accumulators in TMEM):
-//                 S_i(j) = Q_i K_j^T  (SS, M128 N64) into S buffer j % 2 of tile i
-//                 O_i   += P_i(j) V_j (TS: P read from TMEM over that S buffer)
-//               Each tile has two S buffers, so S_i(j+1) (and S_i(j+2) once PV_i(j)
-//               is issued) are computed while the softmax works on S_i(j): the
-//               softmax never waits for a PV -> S round trip, and the two tiles'
-//               work interleaves on the tensor core.
-//   warps 4-7   softmax of Q0, warps 8-11 softmax of Q1; one thread per row:
-//               tcgen05.ld the 64-key S row, row max (3-input max), p = 2^(s*c - m*c)
+//                 S_i = Q_i K_j^T   (SS, M128 N128)          i = 0, 1
+//                 O_i += P_i V_j    (TS: P read from TMEM over S_i's columns)
+//               in the order S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 ...
+//               so the tensor core works on one tile's S / PV while the other
+//               tile's softmax runs (ping-pong).  Because tcgen05.commit tracks
+//               every earlier MMA of the issuing thread, "S_i(j) done" also means
+//               "PV_i(j-1) done": the softmax may touch O_i after that wait.
+//   warps 2-5   softmax of Q0, warps 6-9 softmax of Q1; one thread per row:
+//               tcgen05.ld the S row, row max (3-input max), p = 2^(s*c - m*c)
 //               with packed f32x2 FMAs, row sum, P packed to bf16 and stored with
-//               tcgen05.st over the first half of the S buffer's columns.  3/8 of the
-//               exponentials run on the FMA pipe on tiles without masked keys
-//               (Cody-Waite range reduction and a degree-4 polynomial, relative error
-//               3.1e-6, fitted by least squares on Chebyshev nodes).  O is rescaled
-//               only when a row max grows by more than 2^8 (exact: numerator and
-//               denominator share the stale max), after waiting for the previous PV.
+//               tcgen05.st over the first half of S's columns.  About 3/8 of the
+//               exponentials run on the FMA pipe (Cody-Waite range reduction and a
+//               degree-4 polynomial, relative error 3.1e-6, fitted by least squares
+//               on Chebyshev nodes) so the MUFU unit is not the bottleneck.  O is
+//               rescaled only when a row max grows by more than 2^8 (exact: the
+//               numerator and denominator share the stale max).
 // All mbarrier waits are bounded (sm100.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -41,8 +42,8 @@ namespace {
 using namespace enigma_sm100;
 
 constexpr int BM = 128;            // rows per Q tile (two tiles per CTA)
-constexpr int BN = 64;             // keys per KV tile
-constexpr int KV_STAGES = 4;
+constexpr int BN = 128;            // keys per KV tile
+constexpr int KV_STAGES = 2;
 constexpr int THREADS = 384;       // warpgroup 0: TMA warp, MMA warp, 2 idle; WG 1, 2: softmax
 // Register split (setmaxnreg): the kernel launches with LAUNCH_REGS per thread
 // (384 x 168 = 64512 of the SM's 65536); warpgroup 0 gives back down to WG0_REGS and
@@ -60,9 +61,9 @@ struct Cfg {
   static constexpr int Q_BYTES = BM * D * 2;     // one Q tile
   static constexpr int KV_BYTES = BN * D * 2;    // one K tile == one V tile
   static constexpr int KATOMS = D / 64;          // 128-byte swizzle atoms along D
-  static constexpr int SMEM = 2 * Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 512;
-  static constexpr uint32_t TMEM_COLS = 512;     // S0a S0b S1a S1b (64 each) | O0 | O1
-  static constexpr uint32_t O_COL = 4 * BN;
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = 512;     // S0 | S1 | O0 | O1
+  static constexpr uint32_t O_COL = 2 * BN;
 };
 
 struct Params {
@@ -140,13 +141,9 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint64_t* k_empty = k_full + KV_STAGES;
   uint64_t* v_full = k_empty + KV_STAGES;
   uint64_t* v_empty = v_full + KV_STAGES;
-  uint64_t* s_full = v_empty + KV_STAGES;    // [2 tiles][2 S buffers]
-  // [2 tiles][2 S buffers][2 halves of the keys].  One set per S buffer: the softmax may
-  // run a step ahead of the PV that consumes its previous P, so a single per-tile barrier
-  // could complete two phases before the MMA thread waits on the first.
-  uint64_t* p_full = s_full + 4;
-  uint64_t* pv_done = p_full + 8;            // [2 tiles]: one completion per PV
-  uint64_t* o_done = pv_done + 2;            // [2 tiles]: after the last PV
+  uint64_t* s_full = v_empty + KV_STAGES;    // [2] one per Q tile
+  uint64_t* p_full = s_full + 2;             // [2 tiles][2 halves of the keys]
+  uint64_t* o_done = p_full + 4;             // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5;
@@ -180,10 +177,10 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&p_full[i], 128);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&pv_done[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[2 * i], 128);
+      mbar_init(&p_full[2 * i + 1], 128);
       mbar_init(&o_done[i], 1);
     }
     fence_barrier_init();
@@ -224,17 +221,17 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
     }
     __syncwarp();
-   } else if (warp == 1) {
+  } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_all > 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(BM, BN, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(BM, D, false, true);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       bool ok = mbar_wait(q_full, 0, p.status);
-      // S_i(j) = Q_i K_j^T into S buffer j % 2 of tile i.
+      // S_i(j) = Q_i K_j^T into S buffer i.
       auto issue_s = [&](int i, int j) {
         const int s = j % KV_STAGES;
-        const uint32_t s_tmem = tmem + uint32_t(i * 2 * BN + (j & 1) * BN);
+        const uint32_t s_tmem = tmem + uint32_t(i * BN);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t offq = i * C::Q_BYTES + (kk / 4) * (BM * 128) + (kk % 4) * 32;
@@ -242,54 +239,44 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           mma_bf16_ss(s_tmem, smem_desc_sw128(q_addr + offq, 16, 1024),
                       smem_desc_sw128(k_addr + offk, 16, 1024), idesc_s, kk != 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[2 * i + (j & 1)]);
+        mma_commit(&s_full[i]);
       };
-      // O_i += P_i(j) V_j; P arrives in two halves (keys 0-31, 32-63).
+      // O_i += P_i(j) V_j, P_i(j) read from TMEM over S buffer i.
+      // P arrives in two halves (keys 0-63, 64-127) so the first half's MMAs start while
+      // the softmax finishes the second.
       auto issue_pv = [&](int i, int j) -> bool {
         const int s = j % KV_STAGES;
         if (!mbar_wait(&v_full[s], (j / KV_STAGES) & 1, p.status)) return false;
-        const uint32_t p_tmem = tmem + uint32_t(i * 2 * BN + (j & 1) * BN);
+        const uint32_t p_tmem = tmem + uint32_t(i * BN);
         const uint64_t dv = smem_desc_sw128(v_addr + s * C::KV_BYTES, BN * 128, 1024);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          if (!mbar_wait(&p_full[4 * i + 2 * (j & 1) + half], (j >> 1) & 1, p.status)) return false;
+          if (!mbar_wait(&p_full[2 * i + half], j & 1, p.status)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int kk = half * (BN / 32); kk < (half + 1) * (BN / 32); ++kk)
+          for (int kk = half * 4; kk < half * 4 + 4; ++kk)
             mma_bf16_ts(tmem + C::O_COL + i * D, p_tmem + kk * 8,
                         dv + uint64_t((kk * 2048) >> 4), idesc_o, (j | kk) != 0 ? 1u : 0u);
         }
-        mma_commit(&pv_done[i]);
         return true;
       };
-      auto wait_k = [&](int j) -> bool {
-        if (!mbar_wait(&k_full[j % KV_STAGES], (j / KV_STAGES) & 1, p.status)) return false;
-        tc_fence_after();
-        return true;
-      };
-      // Prologue: S_i(0), S_i(1) for both tiles.
-      for (int j = 0; j < 2 && j < n_all && ok; ++j) {
-        ok = wait_k(j);
-        for (int i = 0; i < 2 && ok; ++i)
-          if (j < n_kv[i]) issue_s(i, j);
-        if (ok) mma_commit(&k_empty[j % KV_STAGES]);
-      }
-      for (int j = 0; j < n_all && ok; ++j) {
-        bool k_ready = false;
+      for (int j = 0; j <= n_all && ok; ++j) {
+        const bool have_k = j < n_all;
+        if (have_k) {
+          if (!mbar_wait(&k_full[j % KV_STAGES], (j / KV_STAGES) & 1, p.status)) break;
+          tc_fence_after();
+        }
+#pragma unroll
         for (int i = 0; i < 2 && ok; ++i) {
-          if (j < n_kv[i]) {
-            ok = issue_pv(i, j);
-            if (ok && j == n_kv[i] - 1) mma_commit(&o_done[i]);
+          if (j >= 1 && j - 1 < n_kv[i]) {
+            ok = issue_pv(i, j - 1);
+            if (ok && j == n_kv[i]) mma_commit(&o_done[i]);
           }
-          // S_i(j+2) reuses S buffer j % 2: issued after PV_i(j), which reads P from it.
-          if (ok && j + 2 < n_kv[i]) {
-            if (!k_ready) ok = k_ready = wait_k(j + 2);
-            if (ok) issue_s(i, j + 2);
-          }
+          if (ok && have_k && j < n_kv[i]) issue_s(i, j);
         }
         if (!ok) break;
-        if (j + 2 < n_all) mma_commit(&k_empty[(j + 2) % KV_STAGES]);
-        mma_commit(&v_empty[j % KV_STAGES]);
+        if (have_k) mma_commit(&k_empty[j % KV_STAGES]);
+        if (j >= 1) mma_commit(&v_empty[(j - 1) % KV_STAGES]);
       }
     }
     __syncwarp();
@@ -302,16 +289,15 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int r = quarter * 32 + lane;        // row of the tile owned by this thread
     const int qi = q0 + ti * BM + r;          // query index
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + uint32_t(ti * BN);
     const uint32_t o_addr = tmem + lane_off + C::O_COL + uint32_t(ti * D);
     const float c = p.scale_log2;
     const int n_my = n_kv[ti];
     float m_used = -INFINITY, l = 0.f;        // m in raw score units
     bool ok = true;
     for (int j = 0; j < n_my && ok; ++j) {
-      const int buf = j & 1;
-      if (!mbar_wait(&s_full[2 * ti + buf], (j >> 1) & 1, p.status)) { ok = false; break; }
+      if (!mbar_wait(&s_full[ti], j & 1, p.status)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t s_addr = tmem + lane_off + uint32_t(ti * 2 * BN + buf * BN);
       float x[BN];
 #pragma unroll
       for (int k = 0; k < BN; k += 16) tmem_ld16(s_addr + k, *reinterpret_cast<uint32_t(*)[16]>(&x[k]));
@@ -329,12 +315,10 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // Row max: four independent 3-input-max chains, then combined.
       float mq[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-      for (int k = 4; k + 8 <= BN; k += 8) {
+      for (int k = 4; k < BN; k += 8) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) mq[u] = max3f(mq[u], x[k + u], x[k + 4 + u]);
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) mq[u] = fmaxf(mq[u], x[BN - 4 + u]);
       const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
       const float m_new = fmaxf(m_used, mx);
       // tcgen05.ld/st are warp-collective: the lazy-rescale decision is taken per warp.
@@ -342,9 +326,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       if (j == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, need)) {
-        // O holds PV_i(0 .. j-2) for sure; wait for PV_i(j-1) before rewriting it.
-        if (!mbar_wait(&pv_done[ti], (j - 1) & 1, p.status)) { ok = false; break; }
-        tc_fence_after();
+        // "S_i(j) done" implies PV_i(j-1) done (commit order), so O is complete here.
         const float f = need ? ex2((m_used - m_new) * c) : 1.0f;   // m_used = -inf: f = 0
         l *= f;
 #pragma unroll 1
@@ -380,11 +362,11 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             sum2 = f2add(sum2, e);
             pk[t] = pack_bf16x2(e.x, e.y);
           }
-          tmem_st8(s_addr + k / 2, pk);        // P (bf16 pairs) over the S buffer's first half
+          tmem_st8(s_addr + k / 2, pk);        // P (bf16 pairs) over S's first 64 columns
           if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[4 * ti + 2 * buf + (k == BN - 16 ? 1 : 0)]);
+            mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
           }
         }
       };
