@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <utility>
 #include <mutex>
 
 #include "common.cuh"
@@ -57,6 +58,7 @@ gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
   uint64_t* acc_full = empty + SK_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = blockIdx.x, split = blockIdx.y;
   const int num_kb = (K + SK_BK - 1) / SK_BK;
@@ -81,6 +83,7 @@ gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // A (the previous kernel's output) and the partial buffer are ready / free
 
   if (warp == 0) {
     if (elect_one()) {
@@ -162,6 +165,8 @@ qkv_finalize_kernel(const float* __restrict__ part, int splits, int M, int N, in
                     const float* __restrict__ cosv, const float* __restrict__ sinv,
                     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kc,
                     __nv_bfloat16* __restrict__ vc, int s_cap, int pos) {
+  griddep_launch_dependents();
+  griddep_wait();
   constexpr int D = 64, H2 = 32;
   const int m = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
   const int c = head * D + d;
@@ -197,6 +202,8 @@ reduce_residual_norm_kernel(const float* __restrict__ part, int splits, int M, i
                             const __nv_bfloat16* __restrict__ residual,
                             __nv_bfloat16* __restrict__ h_out, const __nv_bfloat16* __restrict__ w,
                             __nv_bfloat16* __restrict__ y_out, float eps) {
+  griddep_launch_dependents();
+  griddep_wait();
   constexpr int kPer = 2;  // float4 groups per thread: 256 * 2 * 4 = 2048 columns
   __shared__ float red[8];
   const int m = blockIdx.x;
@@ -254,6 +261,8 @@ reduce_residual_norm_kernel(const float* __restrict__ part, int splits, int M, i
 __global__ void __launch_bounds__(256)
 swiglu_kernel(const float* __restrict__ part, int splits, int M, int I,
               __nv_bfloat16* __restrict__ act) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t q = int64_t(blockIdx.x) * 256 + threadIdx.x;  // float4 group index
   if (q * 4 >= int64_t(M) * I) return;
   const int m = int(q * 4 / I), j = int(q * 4 % I);
@@ -332,6 +341,8 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
                          const __nv_bfloat16* __restrict__ vc, float* __restrict__ opart,
                          float* __restrict__ mlpart, int Hq, int Hkv, int cap, int L, int chunk,
                          float scale_log2) {
+  griddep_launch_dependents();
+  griddep_wait();
   __shared__ __align__(128) uint8_t sv[DA_WARPS][DA_BLOCK * DA_D * 2];   // 8 KB per warp
   const int G = Hq / Hkv;
   const int bhk = blockIdx.x, split = blockIdx.y;
@@ -459,6 +470,8 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
 __global__ void __launch_bounds__(DA_D)
 decode_attn_combine_kernel(const float* __restrict__ opart, const float* __restrict__ mlpart,
                            __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int nparts) {
+  griddep_launch_dependents();
+  griddep_wait();
   __shared__ float wgt[64];
   __shared__ float inv_den;
   const int G = Hq / Hkv;
@@ -507,6 +520,25 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64
 namespace {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Launch with programmatic stream serialization: the kernel may start while its
+// predecessor drains; every decode kernel waits (griddep_wait) before touching memory
+// the predecessor writes or reads.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Split-K factor: about one (tile, split) CTA per SM, at least 2 k-blocks per split.
 int pick_splits(int64_t N, int64_t K, int sms) {
@@ -566,9 +598,8 @@ cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M
   const int kbs = int((K + SK_BK - 1) / SK_BK);
   const int per = (kbs + splits - 1) / splits;
   dim3 grid(unsigned((N + SK_BN - 1) / SK_BN), unsigned(splits));
-  gemm_splitk_tc_kernel<<<grid, SK_THREADS, SK_SMEM, s>>>(ta, tb, partial, int(M), int(N), int(K),
-                                                          per, status);
-  return cudaGetLastError();
+  return launch_pdl(gemm_splitk_tc_kernel, grid, dim3(SK_THREADS), SK_SMEM, s, ta, tb, partial,
+                    int(M), int(N), int(K), per, status);
 }
 
 }  // namespace
@@ -595,41 +626,43 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
   // 2-3. QKV projection, RoPE, KV-cache append at `position`
   int sp = pick_splits(Nqkv, H, sms);
   ENIGMA_TRY(splitk_gemm(bfp(l.xn), d.w_qkv, part, B, Nqkv, H, sp, status, s));
-  qkv_finalize_kernel<<<dim3(B, Hq + 2 * Hkv), 32, 0, s>>>(
-      part, sp, B, Nqkv, Hq, Hkv, d.rope_cos, d.rope_sin, bfp(l.q),
-      static_cast<__nv_bfloat16*>(d.k_cache), static_cast<__nv_bfloat16*>(d.v_cache),
-      int(d.cache_capacity), int(d.position));
-  ENIGMA_TRY(cudaGetLastError());
+  ENIGMA_TRY(launch_pdl(qkv_finalize_kernel, dim3(B, Hq + 2 * Hkv), dim3(32), 0, s,
+                        static_cast<const float*>(part), sp, B, Nqkv, Hq, Hkv, d.rope_cos,
+                        d.rope_sin, bfp(l.q), static_cast<__nv_bfloat16*>(d.k_cache),
+                        static_cast<__nv_bfloat16*>(d.v_cache), int(d.cache_capacity),
+                        int(d.position)));
   // 4-5. attention over position + 1 keys, split-KV then combine
-  decode_attn_split_kernel<<<dim3(B * Hkv, l.attn_splits), DA_WARPS * 32, 0, s>>>(
-      bfp(l.q), static_cast<const __nv_bfloat16*>(d.k_cache),
-      static_cast<const __nv_bfloat16*>(d.v_cache), reinterpret_cast<float*>(w + l.opart),
-      reinterpret_cast<float*>(w + l.mlpart), Hq, Hkv, int(d.cache_capacity),
-      int(d.position + 1), l.attn_chunk, d.attn_scale * 1.4426950408889634f);
-  ENIGMA_TRY(cudaGetLastError());
-  decode_attn_combine_kernel<<<B * Hq, DA_D, 0, s>>>(reinterpret_cast<float*>(w + l.opart),
-                                                      reinterpret_cast<float*>(w + l.mlpart),
-                                                      bfp(l.attn), Hq, Hkv, l.attn_splits * DA_WARPS);
-  ENIGMA_TRY(cudaGetLastError());
+  ENIGMA_TRY(launch_pdl(decode_attn_split_kernel, dim3(B * Hkv, l.attn_splits),
+                        dim3(DA_WARPS * 32), 0, s, static_cast<const __nv_bfloat16*>(bfp(l.q)),
+                        static_cast<const __nv_bfloat16*>(d.k_cache),
+                        static_cast<const __nv_bfloat16*>(d.v_cache),
+                        reinterpret_cast<float*>(w + l.opart),
+                        reinterpret_cast<float*>(w + l.mlpart), Hq, Hkv, int(d.cache_capacity),
+                        int(d.position + 1), l.attn_chunk, d.attn_scale * 1.4426950408889634f));
+  ENIGMA_TRY(launch_pdl(decode_attn_combine_kernel, dim3(B * Hq), dim3(DA_D), 0, s,
+                        static_cast<const float*>(reinterpret_cast<float*>(w + l.opart)),
+                        static_cast<const float*>(reinterpret_cast<float*>(w + l.mlpart)),
+                        bfp(l.attn), Hq, Hkv, l.attn_splits * DA_WARPS));
   // 6-7. O projection + residual(x) -> h1, post-attention RMSNorm -> h1n
   sp = pick_splits(H, Hq * D, sms);
   ENIGMA_TRY(splitk_gemm(bfp(l.attn), d.w_o, part, B, H, Hq * D, sp, status, s));
-  reduce_residual_norm_kernel<<<B, 256, 0, s>>>(part, sp, B, H, xb, bfp(l.h1),
-                                                static_cast<const __nv_bfloat16*>(d.w_post_norm),
-                                                bfp(l.h1n), d.eps);
-  ENIGMA_TRY(cudaGetLastError());
+  ENIGMA_TRY(launch_pdl(reduce_residual_norm_kernel, dim3(B), dim3(256), 0, s,
+                        static_cast<const float*>(part), sp, B, H, xb, bfp(l.h1),
+                        static_cast<const __nv_bfloat16*>(d.w_post_norm), bfp(l.h1n), d.eps));
   // 8-9. gate|up projection, SwiGLU
   sp = pick_splits(2 * I, H, sms);
   ENIGMA_TRY(splitk_gemm(bfp(l.h1n), d.w_gate_up, part, B, 2 * I, H, sp, status, s));
-  swiglu_kernel<<<unsigned((int64_t(B) * I / 4 + 255) / 256), 256, 0, s>>>(part, sp, B, I, bfp(l.act));
-  ENIGMA_TRY(cudaGetLastError());
+  ENIGMA_TRY(launch_pdl(swiglu_kernel, dim3(unsigned((int64_t(B) * I / 4 + 255) / 256)),
+                        dim3(256), 0, s, static_cast<const float*>(part), sp, B, I, bfp(l.act)));
   // 10-11. down projection + residual(h1) -> out
   sp = pick_splits(H, I, sms);
   ENIGMA_TRY(splitk_gemm(bfp(l.act), d.w_down, part, B, H, I, sp, status, s));
-  reduce_residual_norm_kernel<<<B, 256, 0, s>>>(part, sp, B, H, bfp(l.h1),
-                                                static_cast<__nv_bfloat16*>(out), nullptr,
-                                                nullptr, 0.f);
-  ENIGMA_TRY(cudaGetLastError());
+  ENIGMA_TRY(launch_pdl(reduce_residual_norm_kernel, dim3(B), dim3(256), 0, s,
+                        static_cast<const float*>(part), sp, B, H,
+                        static_cast<const __nv_bfloat16*>(bfp(l.h1)),
+                        static_cast<__nv_bfloat16*>(out),
+                        static_cast<const __nv_bfloat16*>(nullptr),
+                        static_cast<__nv_bfloat16*>(nullptr), 0.f));
 #undef ENIGMA_TRY
   return cudaSuccess;
 }
