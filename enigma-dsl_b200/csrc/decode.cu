@@ -47,7 +47,7 @@ constexpr int SK_THREADS = 192;
 __global__ void __launch_bounds__(SK_THREADS)
 gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       float* __restrict__ partial, int M, int N, int K, int kb_per_split,
-                      uint32_t* status) {
+                      int a_rows, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -79,6 +79,16 @@ gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
     tmem_alloc(tmem_slot, SK_BN);
     tmem_relinquish();
   }
+  // The TMA box covers the a_rows (= M rounded up to 8) real rows of A; the MMA reads 128.
+  // Rows a_rows..127 of every A stage are zeroed once here (128-byte rows, swizzle only
+  // permutes 16-byte chunks within a row, so whole rows stay zero) and never written again.
+  if (a_rows < SK_BM) {
+    for (int i = threadIdx.x; i < SK_STAGES * (SK_BM - a_rows) * 8; i += SK_THREADS) {
+      const int st = i / ((SK_BM - a_rows) * 8), rem = i % ((SK_BM - a_rows) * 8);
+      reinterpret_cast<uint4*>(sA + st * SK_A_BYTES + a_rows * 128)[rem] = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -90,7 +100,7 @@ gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
       for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
         const int s = i % SK_STAGES;
         if (!mbar_wait(&empty[s], ((i / SK_STAGES) & 1) ^ 1, status)) break;
-        mbar_arrive_expect_tx(&full[s], SK_STAGE);
+        mbar_arrive_expect_tx(&full[s], a_rows * SK_BK * 2 + SK_B_BYTES);
         tma_load_2d(sA + s * SK_A_BYTES, &tmA, &full[s], kb * SK_BK, 0);
         tma_load_2d(sB + s * SK_B_BYTES, &tmB, &full[s], nb * SK_BN, kb * SK_BK);
       }
@@ -589,7 +599,8 @@ Layout plan(const enigma_decode_layer_desc& d, int sms) {
 cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M, int64_t N,
                         int64_t K, int splits, uint32_t* status, cudaStream_t s) {
   CUtensorMap ta, tb;
-  if (!make_tmap_bf16_2d(&ta, A, M, K, K, SK_BK, SK_BM) ||
+  const int a_rows = int(std::min<int64_t>(SK_BM, (M + 7) / 8 * 8));
+  if (!make_tmap_bf16_2d(&ta, A, M, K, K, SK_BK, uint32_t(a_rows)) ||
       !make_tmap_bf16_2d(&tb, Bw, K, N, N, SK_BN, SK_BK))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(gemm_splitk_tc_kernel,
@@ -599,7 +610,7 @@ cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M
   const int per = (kbs + splits - 1) / splits;
   dim3 grid(unsigned((N + SK_BN - 1) / SK_BN), unsigned(splits));
   return launch_pdl(gemm_splitk_tc_kernel, grid, dim3(SK_THREADS), SK_SMEM, s, ta, tb, partial,
-                    int(M), int(N), int(K), per, status);
+                    int(M), int(N), int(K), per, a_rows, status);
 }
 
 }  // namespace
