@@ -81,6 +81,32 @@ class _Trace:
             return self.const_of(op.operands[0])
         return None
 
+    def source_of(self, v):
+        """Where a scalar operand comes from: a literal (float), a Scalar kernel
+        parameter ({"scalar": buffer_index}) or a function constant ({"constant": index});
+        None otherwise.  Lets eps / scale be runtime values (runtime.py:125-175, :358-364)."""
+        c = self.const_of(v)
+        if c is not None:
+            return float(c)
+        op = self.def_of(v)
+        while op is not None and op.op == "cast":
+            op = self.def_of(op.operands[0])
+        if op is None:
+            return None
+        if op.op == "function_constant":
+            return {"constant": int(op.attrs["index"])}
+        if op.op == "load" and any(sp[1] == op.attrs.get("buffer_index") for sp in
+                                   self.b.scalar_params):
+            return {"scalar": int(op.attrs["buffer_index"])}
+        return None
+
+    def n_buffers(self) -> int:
+        return len(self.b.args) - len(self.b.scalar_params)
+
+    def buffer_dtypes(self):
+        scal = {sp[1] for sp in self.b.scalar_params}
+        return [a[2] for a in self.b.args if a[1] not in scal]
+
     def def_of(self, v):
         return self.producer.get(id(v)) if isinstance(v, IRValue) else None
 
@@ -102,10 +128,10 @@ def _rmsnorm_eps(t: _Trace) -> Tuple[Optional[float], Optional[float]]:
         if add is None or add.op not in ("add", "tv_add"):
             continue
         a, b = add.operands
-        eps = t.const_of(b)
+        eps = t.source_of(b)
         mean = t.def_of(a)
         if eps is None:
-            eps, mean = t.const_of(a), t.def_of(b)
+            eps, mean = t.source_of(a), t.def_of(b)
         n = None
         if mean is not None and mean.op in ("div", "tv_div"):
             n = t.const_of(mean.operands[1])
@@ -114,17 +140,17 @@ def _rmsnorm_eps(t: _Trace) -> Tuple[Optional[float], Optional[float]]:
 
 
 def _match_rmsnorm(t: _Trace, args: tuple) -> Optional[Binding]:
-    if len(t.b.args) != 3 or not t.has("rsqrt", "simd_sum"):
+    if t.n_buffers() != 3 or not t.has("rsqrt", "simd_sum"):
         return None
     if t.kinds["exp"] or t.kinds["dot"]:
         return None
     eps, n = _rmsnorm_eps(t)
     if eps is None:
         return None
-    dtypes = {a[2] for a in t.b.args}
+    dtypes = set(t.buffer_dtypes())
     if len(dtypes) != 1 or not dtypes <= {"float", "bfloat"}:
         return None
-    params = {"eps": float(eps)}
+    params = {"eps": eps}
     if n:
         params["hidden"] = int(n)
     x = _first_tensor(args, 2)
@@ -149,9 +175,9 @@ def _first_tensor(args, rank: int) -> Optional[Tensor]:
 
 # ----------------------------------------------------------------------------- sdpa
 def _match_sdpa(t: _Trace, args: tuple) -> Optional[Binding]:
-    if len(t.b.args) != 4 or not t.has("exp", "fmax"):
+    if t.n_buffers() != 4 or not t.has("exp", "fmax"):
         return None
-    dtype = t.b.args[0][2]
+    dtype = t.buffer_dtypes()[0]
     if dtype not in ("float", "bfloat"):
         return None
     if t.has("simd_sum", "dot", "threadgroup_alloc"):
@@ -167,6 +193,12 @@ def _match_sdpa(t: _Trace, args: tuple) -> Optional[Binding]:
                 c = t.const_of(op.operands[0])
                 if c:
                     scale = 1.0 / math.sqrt(c)
+            elif op.op in ("mul", "tv_mul") and scale is None:
+                # score * scale with the scale a Scalar parameter or function constant
+                for o in op.operands:
+                    src = t.source_of(o)
+                    if isinstance(src, dict):
+                        scale = src
         params = {"scale": scale if scale is not None else 1.0, "causal": False}
         if d:
             params["head_dim"] = d

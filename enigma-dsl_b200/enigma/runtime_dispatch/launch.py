@@ -38,7 +38,31 @@ def _div(nbytes: int, per: int, what: str) -> int:
     return nbytes // per
 
 
-def plan(binding, nbytes: List[int], grid: Tuple[int, ...], threads: Tuple[int, ...]) -> LaunchPlan:
+def resolve(v, values):
+    """A bound parameter: a number, or {"scalar": slot} / {"constant": index} looked up in
+    this dispatch's scalar values and function constants."""
+    if isinstance(v, dict):
+        if "scalar" in v:
+            table, key, what = (values or {}).get("scalars", {}), v["scalar"], "Scalar parameter"
+        else:
+            table, key, what = (values or {}).get("constants", {}), v["constant"], \
+                "function constant"
+        _need(key in table, f"{what} {key} has no value: pass it with scalars= / constants=")
+        return float(table[key])
+    return float(v)
+
+
+def plan(binding, nbytes: List[int], grid: Tuple[int, ...], threads: Tuple[int, ...],
+         values=None) -> LaunchPlan:
+    """`nbytes` lists the device buffers in bind order without Scalar slots; `values`
+    holds {"scalars": {slot: value}, "constants": {index: value}} of this dispatch."""
+    if values is None and any(isinstance(v, dict) for v in binding.params.values()):
+        _need(False, "this kernel takes Scalar parameters / function constants: dispatch it with "
+                     "execute(..., scalars=..., constants=...)")
+    if values:
+        binding = type(binding)(binding.op, binding.dtype,
+                                {k: (resolve(v, values) if isinstance(v, dict) else v)
+                                 for k, v in binding.params.items()}, binding.layout)
     op = binding.op
     if op == "rmsnorm":
         return _plan_rmsnorm(binding, nbytes)

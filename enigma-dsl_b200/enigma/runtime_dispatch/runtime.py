@@ -233,11 +233,17 @@ class MetalRuntime:
         self._check_bind_count("execute", compiled, len(inputs), len(scalars or []),
                                len(out_sizes))
         merged = _merge_scalar_buffers(inputs, scalars or [], scalar_params, len(out_sizes))
+        scalar_slots = {sp[1] for sp in scalar_params}
+        values = {"scalars": {sp[1]: v for sp, v in zip(scalar_params, scalars or [])},
+                  "constants": {int(k): (v[1] if isinstance(v, tuple) else v)
+                                for k, v in (constants or {}).items()}}
         bufs = self._bind(merged, out_sizes)
         try:
-            p = _launch.plan(binding, bufs.nbytes, tuple(grid), tuple(threads))
+            keep = [i for i in range(len(bufs.ptrs)) if i not in scalar_slots]
+            p = _launch.plan(binding, [bufs.nbytes[i] for i in keep], tuple(grid), tuple(threads),
+                             values)
             try:
-                p.fn(bufs.ptrs, self._stream)
+                p.fn([bufs.ptrs[i] for i in keep], self._stream)
                 _native.call("enigma_synchronize", self._stream)
             except _native.EnigmaCudaError as e:
                 raise _gpu_error(f"dispatch failed: {e}", kernel=compiled.kernel_name, grid=grid,

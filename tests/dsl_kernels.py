@@ -368,3 +368,43 @@ def make_naive_binary(op):
         i = enigma.thread_position_in_grid
         C[i] = op(A[i], B[i])
     return binary
+
+
+# ---------------------------------------------------------------- RMSNorm with runtime eps
+# One threadgroup per row, strided loop over the row (the layout of the Qwen layer's
+# _rmsnorm, qwen_megakernel.py:41-66), eps given as a Scalar parameter or a function constant.
+def make_rmsnorm_runtime_eps(hidden, mode, TG=256):
+    def u(v):
+        return enigma.metal_cast(v, "uint")
+
+    def body(X, W, Y, eps):
+        row = enigma.threadgroup_position_in_grid("x")
+        tid = enigma.thread_position_in_threadgroup()
+        base = row * u(hidden)
+        lane = enigma.thread_index_in_simdgroup()
+        sg = enigma.simdgroup_index_in_threadgroup()
+        z = enigma.metal_cast(0, "float")
+        with enigma.for_range(0, hidden // TG, init=[z]) as (j, c):
+            v = X[base + tid + u(j) * u(TG)]
+            c[0] = c[0] + v * v
+        scratch = enigma.threadgroup_alloc("float", 32)
+        enigma.store_if(scratch, sg, enigma.simd_sum(c[0]), enigma.cmp_eq(lane, 0))
+        enigma.barrier()
+        tot = enigma.simd_sum(enigma.load_if(scratch, lane, enigma.cmp_ult(
+            lane, enigma.simdgroups_per_threadgroup()), default=0.0))
+        r = enigma.rsqrt(tot / float(hidden) + eps)
+        with enigma.for_range(0, hidden // TG) as j:
+            i = tid + u(j) * u(TG)
+            Y[base + i] = X[base + i] * r * W[i]
+
+    if mode == "scalar":
+        @enigma.kernel
+        def rmsnorm_scalar_eps(X: enigma.f32, W: enigma.f32, eps: enigma.Scalar(enigma.f32),
+                               Y: enigma.f32):
+            body(X, W, Y, eps)
+        return rmsnorm_scalar_eps
+
+    @enigma.kernel
+    def rmsnorm_const_eps(X: enigma.f32, W: enigma.f32, Y: enigma.f32):
+        body(X, W, Y, enigma.function_constant("float", 0))
+    return rmsnorm_const_eps

@@ -178,3 +178,17 @@ def test_naive_add(rt, n):
     a, b = (rng.standard_normal(n).astype(np.float32) for _ in range(2))
     raw = rt.execute(ck, [a, b], a.nbytes, grid=(n, 1, 1), threads=(min(n, 256), 1, 1))
     np.testing.assert_allclose(np.frombuffer(raw, np.float32), a + b, rtol=1e-5)
+
+
+@pytest.mark.parametrize("mode", ["scalar", "constant"])
+def test_rmsnorm_runtime_eps(rt, mode):
+    """eps as a Scalar parameter (runtime.py:125-175) or a function constant (:358-364)."""
+    ck = enigma.compile(K.make_rmsnorm_runtime_eps(1024, mode))
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((64, 1024)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    kw = {"scalars": [1e-2]} if mode == "scalar" else {"constants": {0: ("float", 1e-2)}}
+    raw = rt.execute(ck, [x.ravel(), w], x.nbytes, grid=(64 * 256, 1, 1), threads=(256, 1, 1),
+                     **kw)
+    np.testing.assert_allclose(np.frombuffer(raw, np.float32).reshape(64, 1024),
+                               orc.rmsnorm(x, w, 1e-2), rtol=1e-5, atol=1e-6)

@@ -87,3 +87,23 @@ def test_tv_add_binding():
 def test_naive_binary_binding(fn, code):
     b = enigma.compile(K.make_naive_binary(fn)).cuda_kernel
     assert (b.op, b.layout, b.params["op"]) == ("elementwise", "naive", code)
+
+
+def test_runtime_eps_bindings():
+    b = enigma.compile(K.make_rmsnorm_runtime_eps(1024, "scalar")).cuda_kernel
+    assert b.op == "rmsnorm" and b.params["eps"] == {"scalar": 2} and b.params["hidden"] == 1024
+    b = enigma.compile(K.make_rmsnorm_runtime_eps(1024, "constant")).cuda_kernel
+    assert b.params["eps"] == {"constant": 0}
+
+
+def test_runtime_eps_resolution():
+    from enigma.runtime_dispatch import launch
+    b = enigma.compile(K.make_rmsnorm_runtime_eps(1024, "scalar")).cuda_kernel
+    p = launch.plan(b, [8 * 1024 * 4, 1024 * 4, 8 * 1024 * 4], (8 * 256, 1, 1), (256, 1, 1),
+                    {"scalars": {2: 1e-3}, "constants": {}})
+    assert "eps=0.001" in p.describe
+    with pytest.raises(RuntimeError, match="Scalar parameter 2 has no value"):
+        launch.plan(b, [8 * 1024 * 4, 1024 * 4, 8 * 1024 * 4], (1, 1, 1), (1, 1, 1),
+                    {"scalars": {}, "constants": {}})
+    with pytest.raises(RuntimeError, match="execute"):
+        launch.plan(b, [8 * 1024 * 4, 1024 * 4, 8 * 1024 * 4], (1, 1, 1), (1, 1, 1))
