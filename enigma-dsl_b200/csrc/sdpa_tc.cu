@@ -142,8 +142,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint64_t* v_full = k_empty + KV_STAGES;
   uint64_t* v_empty = v_full + KV_STAGES;
   uint64_t* s_full = v_empty + KV_STAGES;    // [2] one per Q tile
-  uint64_t* p_full = s_full + 2;             // [2 tiles][2 halves of the keys]
-  uint64_t* o_done = p_full + 4;             // [2]
+  uint64_t* p_full = s_full + 2;             // [2 tiles][4 quarters of the keys]
+  uint64_t* o_done = p_full + 8;             // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5;
@@ -179,8 +179,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[2 * i], 128);
-      mbar_init(&p_full[2 * i + 1], 128);
+      for (int q = 0; q < 4; ++q) mbar_init(&p_full[4 * i + q], 128);
       mbar_init(&o_done[i], 1);
     }
     fence_barrier_init();
@@ -250,11 +249,11 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const uint32_t p_tmem = tmem + uint32_t(i * BN);
         const uint64_t dv = smem_desc_sw128(v_addr + s * C::KV_BYTES, BN * 128, 1024);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          if (!mbar_wait(&p_full[2 * i + half], j & 1, p.status)) return false;
+        for (int qtr = 0; qtr < 4; ++qtr) {
+          if (!mbar_wait(&p_full[4 * i + qtr], j & 1, p.status)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int kk = half * 4; kk < half * 4 + 4; ++kk)
+          for (int kk = qtr * 2; kk < qtr * 2 + 2; ++kk)
             mma_bf16_ts(tmem + C::O_COL + i * D, p_tmem + kk * 8,
                         dv + uint64_t((kk * 2048) >> 4), idesc_o, (j | kk) != 0 ? 1u : 0u);
         }
@@ -300,7 +299,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       tc_fence_after();
       float x[BN];
 #pragma unroll
-      for (int k = 0; k < BN; k += 16) tmem_ld16(s_addr + k, *reinterpret_cast<uint32_t(*)[16]>(&x[k]));
+      for (int k = 0; k < BN; k += 32) tmem_ld32(s_addr + k, reinterpret_cast<uint32_t*>(&x[k]));
       tmem_wait_ld();
       // Keys past the sequence end and, for causal, past this row's diagonal are masked.
       const int k0 = j * BN;
@@ -348,7 +347,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
       const float mc = (m_used == -INFINITY) ? 0.f : m_used * c;
       const float2 cc = make_float2(c, c), nmc = make_float2(-mc, -mc);
-      float2 sum2 = make_float2(0.f, 0.f);
+      float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};    // four independent accumulation chains
       // exp, row sum, P store; with POLY, 3 of every 8 pairs run on the FMA pipe.
       auto exp_store = [&](auto poly_tag) {
         constexpr bool POLY = decltype(poly_tag)::value;
@@ -359,14 +359,14 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           for (int t = 0; t < 8; ++t) {
             const float2 y = f2fma(make_float2(x[k + 2 * t], x[k + 2 * t + 1]), cc, nmc);
             const float2 e = (POLY && t >= 5) ? ex2_poly2(y) : make_float2(ex2(y.x), ex2(y.y));
-            sum2 = f2add(sum2, e);
+            sum2[t & 3] = f2add(sum2[t & 3], e);
             pk[t] = pack_bf16x2(e.x, e.y);
           }
           tmem_st8(s_addr + k / 2, pk);        // P (bf16 pairs) over S's first 64 columns
-          if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
+          if ((k & 31) == 16) {                  // a quarter of the keys is done: release it
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
+            mbar_arrive(&p_full[4 * ti + (k >> 5)]);
           }
         }
       };
@@ -375,7 +375,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       } else {
         exp_store(std::true_type{});
       }
-      l += sum2.x + sum2.y;
+      const float2 s01 = f2add(sum2[0], sum2[1]), s23 = f2add(sum2[2], sum2[3]);
+      l += (s01.x + s23.x) + (s01.y + s23.y);
     }
     // Epilogue: O / l, bf16, straight to global (each thread one 2*D-byte row).
     if (ok && n_my > 0) ok = mbar_wait(&o_done[ti], 0, p.status);
