@@ -142,8 +142,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint64_t* v_full = k_empty + KV_STAGES;
   uint64_t* v_empty = v_full + KV_STAGES;
   uint64_t* s_full = v_empty + KV_STAGES;    // [2] one per Q tile
-  uint64_t* p_full = s_full + 2;             // [2 tiles][4 quarters of the keys]
-  uint64_t* o_done = p_full + 8;             // [2]
+  uint64_t* p_full = s_full + 2;             // [2 tiles][2 halves of the keys]
+  uint64_t* o_done = p_full + 4;             // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5;
@@ -179,7 +179,8 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      for (int q = 0; q < 4; ++q) mbar_init(&p_full[4 * i + q], 128);
+      mbar_init(&p_full[2 * i], 128);
+      mbar_init(&p_full[2 * i + 1], 128);
       mbar_init(&o_done[i], 1);
     }
     fence_barrier_init();
@@ -249,11 +250,11 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const uint32_t p_tmem = tmem + uint32_t(i * BN);
         const uint64_t dv = smem_desc_sw128(v_addr + s * C::KV_BYTES, BN * 128, 1024);
 #pragma unroll
-        for (int qtr = 0; qtr < 4; ++qtr) {
-          if (!mbar_wait(&p_full[4 * i + qtr], j & 1, p.status)) return false;
+        for (int half = 0; half < 2; ++half) {
+          if (!mbar_wait(&p_full[2 * i + half], j & 1, p.status)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int kk = qtr * 2; kk < qtr * 2 + 2; ++kk)
+          for (int kk = half * 4; kk < half * 4 + 4; ++kk)
             mma_bf16_ts(tmem + C::O_COL + i * D, p_tmem + kk * 8,
                         dv + uint64_t((kk * 2048) >> 4), idesc_o, (j | kk) != 0 ? 1u : 0u);
         }
@@ -363,10 +364,10 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             pk[t] = pack_bf16x2(e.x, e.y);
           }
           tmem_st8(s_addr + k / 2, pk);        // P (bf16 pairs) over S's first 64 columns
-          if ((k & 31) == 16) {                  // a quarter of the keys is done: release it
+          if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[4 * ti + (k >> 5)]);
+            mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
           }
         }
       };
