@@ -93,11 +93,24 @@ gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // B (weights) never depends on the previous kernel: the first stages' B tiles go to
+  // shared memory and the rest of this CTA's slice to L2 before waiting on the
+  // predecessor, so the weight stream overlaps its tail.
+  const int pre = min(SK_STAGES, max(0, kb1 - kb0));
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], a_rows * SK_BK * 2 + SK_B_BYTES);
+      tma_load_2d(sB + i * SK_B_BYTES, &tmB, &full[i], nb * SK_BN, (kb0 + i) * SK_BK);
+    }
+    for (int kb = kb0 + pre; kb < kb1; ++kb) tma_prefetch_l2_2d(&tmB, nb * SK_BN, kb * SK_BK);
+  }
   griddep_wait();  // A (the previous kernel's output) and the partial buffer are ready / free
 
   if (warp == 0) {
-    if (elect_one()) {
-      for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
+    if (lane == 0) {
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(sA + i * SK_A_BYTES, &tmA, &full[i], (kb0 + i) * SK_BK, 0);
+      for (int kb = kb0 + pre, i = pre; kb < kb1; ++kb, ++i) {
         const int s = i % SK_STAGES;
         if (!mbar_wait(&empty[s], ((i / SK_STAGES) & 1) ^ 1, status)) break;
         mbar_arrive_expect_tx(&full[s], a_rows * SK_BK * 2 + SK_B_BYTES);
@@ -352,10 +365,20 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
                          float* __restrict__ mlpart, int Hq, int Hkv, int cap, int L, int chunk,
                          float scale_log2) {
   griddep_launch_dependents();
-  griddep_wait();
   __shared__ __align__(128) uint8_t sv[DA_WARPS][DA_BLOCK * DA_D * 2];   // 8 KB per warp
   const int G = Hq / Hkv;
   const int bhk = blockIdx.x, split = blockIdx.y;
+  // The cached keys before the appended one are not written by the predecessor: pull
+  // this CTA's K and V rows into L2 while it finishes (the new row is read after the wait).
+  if (threadIdx.x == 0) {
+    const int c0 = split * chunk, c1 = min(L - 1, c0 + chunk);
+    if (c1 > c0) {
+      const int64_t off = (int64_t(bhk) * cap + c0) * DA_D;
+      bulk_prefetch_l2(kc + off, uint32_t(c1 - c0) * DA_D * 2);
+      bulk_prefetch_l2(vc + off, uint32_t(c1 - c0) * DA_D * 2);
+    }
+  }
+  griddep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int parts = gridDim.y * DA_WARPS, part = split * DA_WARPS + warp;
   const int b = bhk / Hkv, kvh = bhk % Hkv;

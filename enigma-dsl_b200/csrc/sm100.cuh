@@ -100,6 +100,20 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, ui
       : "memory");
 }
 
+// 2-D tile of a tensor map fetched into L2 only (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* desc, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+               ::"l"(reinterpret_cast<uint64_t>(desc)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// Contiguous bytes fetched into L2 (addr 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* addr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+               ::"l"(reinterpret_cast<uint64_t>(addr)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* desc, uint64_t* bar,
                                             int32_t c0, int32_t c1, int32_t c2) {
   asm volatile(
