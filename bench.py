@@ -154,14 +154,15 @@ def _time_device(fn, steps, stream):
 
 def _time_device_flushed(fn, steps, stream):
     """Average device ms of fn() with L2 flushed before every launch: a 256 MB buffer
-    (twice the 126 MB L2) is overwritten between steps, outside the events, so each
-    step reads its inputs from HBM."""
+    (twice the 126 MB L2) is read between steps, outside the events, so each step reads
+    its inputs from HBM.  The flush reads rather than writes: a written buffer would leave
+    L2 full of dirty lines whose write-back the timed step would pay for."""
     import torch
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = torch.ones(64 << 20, dtype=torch.int32, device="cuda")
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(steps)]
     for s, e in evs:
-        flush.fill_(1)
+        flush.max()
         s.record(stream)
         fn()
         e.record(stream)
@@ -264,7 +265,7 @@ def _decode_side(hbm_peak):
     return {"ms": round(ms, 4), "tokens_per_s": round(cfg.batch / (ms * 1e-3), 1),
             "algorithmic_bytes": byts, "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
             "frac_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm_peak, 4),
-            "l2": "flushed (256 MB write) before every step",
+            "l2": "flushed (256 MB read) before every step",
             "ms_back_to_back": round(ms_warm, 4),
             "note": "weights + KV read once per step; back to back, L2 (126 MB) can hold "
                     "part of the 97 MB working set"}

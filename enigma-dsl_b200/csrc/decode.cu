@@ -176,8 +176,6 @@ gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_cons
 }
 
 // ============================================================================ reductions
-__device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
-
 // q / k / v = sum over splits of the QKV partials; RoPE on the q and k heads
 // (rotate-half pairing d <-> d + D/2 with full-length cos / sin tables, as in
 // examples/qwen_megakernel.py:90-107); q to q_out [M, Hq, D], k and v appended
@@ -187,11 +185,14 @@ __global__ void __launch_bounds__(32)
 qkv_finalize_kernel(const float* __restrict__ part, int splits, int M, int N, int Hq, int Hkv,
                     const float* __restrict__ cosv, const float* __restrict__ sinv,
                     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kc,
-                    __nv_bfloat16* __restrict__ vc, int s_cap, int pos) {
+                    __nv_bfloat16* __restrict__ vc, int s_cap, int pos,
+                    uint32_t* __restrict__ attn_counters) {
   griddep_launch_dependents();
   griddep_wait();
   constexpr int D = 64, H2 = 32;
   const int m = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
+  // The attention kernel's per-(sequence, kv head) completion counters start at zero.
+  if (head >= Hq && head < Hq + Hkv && d == 0) attn_counters[m * Hkv + head - Hq] = 0u;
   const int c = head * D + d;
   float lo = 0.f, hi = 0.f;
   for (int s = 0; s < splits; ++s) {
@@ -305,48 +306,56 @@ swiglu_kernel(const float* __restrict__ part, int splits, int M, int I,
 // ============================================================================ decode attention
 constexpr int DA_D = 64;
 
-// d = a * b + c on two fp32 lanes at once (sm_100 packed FMA).
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-
 __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-// Split-KV decode attention on the tensor cores (mma.sync m16n8k16, bf16 -> fp32).
-// CTA = (sequence b, kv head, key chunk); each of its 4 warps owns a contiguous quarter
-// of the chunk and writes its own unnormalised partial (max, sum, o) for the G <= 8
-// query heads of the group; the combine kernel merges all partials.
-//
-// Per 64-key block a warp computes S = Q K^T (Q = the group's heads as the 16-row A
-// operand, rows >= G zero; K as the B operand straight from global memory), an online
-// softmax in the log2 domain, and O += P V with P taken from the S accumulators and V
-// staged through shared memory (cp.async, XOR-swizzled rows) and read by ldmatrix.trans.
-// The head dimension is consumed in a permuted order: for k-step ks, lane quad t holds
-// fragment columns {2t, 2t+1, 2t+8, 2t+9} = physical dims 16t + 4ks + {0..3}, applied to
-// both Q and K (a dot product is order-free), so each lane reads its K row slice as two
-// contiguous 16-byte loads.
-//   q [B, Hq, D] bf16 (RoPE applied); kc / vc [B, Hkv, cap, D] bf16; L keys valid
-//   opart [B*Hkv, parts, G, D] fp32, mlpart [B*Hkv, parts, G, 2] (max in log2 units, sum)
-constexpr int DA_WARPS = 4;
-constexpr int DA_BLOCK = 64;       // keys per inner step
+// Split-KV decode attention on the tensor cores (mma.sync m16n8k16, bf16 -> fp32), as a
+// persistent kernel.  The work is the flattened list of (unit = sequence b x kv head,
+// 128-key chunk) pairs; CTA c of P takes the contiguous range [c T / P, (c + 1) T / P),
+// so every SM streams the same number of chunks whatever the batch and head counts.
+//   * Warp 4 is the producer: one TMA box of K and one of V per chunk (128 rows x 128 B,
+//     128-byte swizzle) into a DA_NST-stage ring.  Chunks that do not hold the key
+//     appended by the predecessor are requested before the programmatic-launch wait.
+//   * Warps 0..3 each take 32 keys of every chunk:
+//       S = Q K^T  (Q = the group's G <= 8 heads as the 16-row A operand, rows >= G zero;
+//                  K from shared memory by ldmatrix),
+//       online softmax in the log2 domain over the chunks of one unit,
+//       O += P V   (V by ldmatrix.trans).
+//   * At the end of a unit's run of chunks (a "segment") the warps merge in shared memory
+//     into one (m, l, O) partial stored in the slot of the segment's first chunk; the other
+//     slots of the segment are marked empty (m = -inf).  A device-scope counter per unit
+//     (zeroed by the QKV finalize kernel of the same step) counts finished chunks; the CTA
+//     that completes the count merges the unit's partials and writes the bf16 output.
+//   q [B, Hq, D] bf16 (RoPE applied); K / V cache maps over [B*Hkv*cap, D] bf16; L keys
+//   opart [B*Hkv, S, G, D] fp32, mlpart [B*Hkv, S, G, 2] (max in log2 units, sum)
+//   out [B, Hq, D] bf16
+constexpr int DA_KEYS = 128;
+constexpr int DA_WARPS = 4;                        // consumer warps
+constexpr int DA_THREADS = (DA_WARPS + 1) * 32;    // + the producer warp
+constexpr int DA_NST = 3;
+constexpr int DA_TILE = DA_KEYS * DA_D * 2;        // 16 KB: one of K or V
+constexpr int DA_STAGE = 2 * DA_TILE;
+constexpr int DA_MERGE = DA_WARPS * 8 * DA_D * 4;  // 8 KB: warp partials, then the weights
+constexpr int DA_SMEM = DA_NST * DA_STAGE + DA_MERGE + 1024;
+constexpr int DA_CTAS_PER_SM = 2;
 
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a2,
                                                uint32_t b0, uint32_t b1) {
+  // A rows 8..15 (registers a1, a3) are zero: the group has at most 8 query heads.
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
 }
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
@@ -355,92 +364,139 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
+// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile (1024-aligned base).
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+// Named barrier over the consumer warps only (the producer never joins it).
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(DA_WARPS * 32) : "memory");
 }
 
-__global__ void __launch_bounds__(DA_WARPS * 32)
-decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
-                         const __nv_bfloat16* __restrict__ vc, float* __restrict__ opart,
-                         float* __restrict__ mlpart, int Hq, int Hkv, int cap, int L, int chunk,
-                         float scale_log2) {
-  griddep_launch_dependents();
-  __shared__ __align__(128) uint8_t sv[DA_WARPS][DA_BLOCK * DA_D * 2];   // 8 KB per warp
+__global__ void __launch_bounds__(DA_THREADS)
+decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const __nv_bfloat16* __restrict__ q, float* __restrict__ opart,
+                   float* __restrict__ mlpart, uint32_t* __restrict__ counters,
+                   __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int cap, int L, int S,
+                   int units, float scale_log2, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* s_o = reinterpret_cast<float*>(stages + DA_NST * DA_STAGE);   // [warp][8][D]
+  __shared__ uint64_t full[DA_NST], empty[DA_NST];
+  __shared__ float s_m[DA_WARPS][8], s_l[DA_WARPS][8];
+  __shared__ uint32_t s_last;
   const int G = Hq / Hkv;
-  const int bhk = blockIdx.x, split = blockIdx.y;
-  // The cached keys before the appended one are not written by the predecessor: pull
-  // this CTA's K and V rows into L2 while it finishes (the new row is read after the wait).
-  if (threadIdx.x == 0) {
-    const int c0 = split * chunk, c1 = min(L - 1, c0 + chunk);
-    if (c1 > c0) {
-      const int64_t off = (int64_t(bhk) * cap + c0) * DA_D;
-      bulk_prefetch_l2(kc + off, uint32_t(c1 - c0) * DA_D * 2);
-      bulk_prefetch_l2(vc + off, uint32_t(c1 - c0) * DA_D * 2);
-    }
-  }
-  griddep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int parts = gridDim.y * DA_WARPS, part = split * DA_WARPS + warp;
-  const int b = bhk / Hkv, kvh = bhk % Hkv;
-  const int g = lane >> 2, t = lane & 3;
-  const int per_warp = (chunk + DA_WARPS - 1) / DA_WARPS;
-  const int k0 = split * chunk + warp * per_warp;
-  const int k1 = min(L, min(split * chunk + chunk, k0 + per_warp));
+  const int64_t n_chunks = int64_t(S) * units;
+  const int64_t c_begin = n_chunks * blockIdx.x / gridDim.x;
+  const int64_t c_end = n_chunks * (blockIdx.x + 1) / gridDim.x;
 
-  // Q fragments (A operand): row g = head g of the group (rows >= G and rows 8..15 zero).
-  uint32_t qa[4][4];
-  {
-    const bool live = g < G;
-    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-        q + (int64_t(b) * Hq + kvh * G + (live ? g : 0)) * DA_D + 16 * t);
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      qa[ks][0] = live ? qrow[2 * ks] : 0u;
-      qa[ks][2] = live ? qrow[2 * ks + 1] : 0u;
-      qa[ks][1] = 0u;
-      qa[ks][3] = 0u;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    for (int s = 0; s < DA_NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], DA_WARPS);
     }
+    fence_barrier_init();
   }
-  const __nv_bfloat16* kbase = kc + int64_t(bhk) * cap * DA_D;
-  const __nv_bfloat16* vbase = vc + int64_t(bhk) * cap * DA_D;
-  const uint32_t sv_addr = smem_u32(sv[warp]);
+  __syncthreads();
+  griddep_launch_dependents();
 
+  if (warp == DA_WARPS) {                       // ---------------- producer
+    if (lane == 0) {
+      auto issue = [&](int64_t ci, int st) {
+        const int32_t row = int32_t((ci / S) * cap + (ci % S) * DA_KEYS);
+        uint8_t* dst = stages + st * DA_STAGE;
+        mbar_arrive_expect_tx(&full[st], DA_STAGE);
+        tma_load_2d(dst, &tmK, &full[st], 0, row);
+        tma_load_2d(dst + DA_TILE, &tmV, &full[st], 0, row);
+      };
+      // Before the wait: the first stages and an L2 prefetch of the rest of the range,
+      // stopping at the first chunk that holds an appended key (the last of a unit).
+      int64_t ci = c_begin;
+      int i = 0;
+      for (; ci < c_end && i < DA_NST && ci % S != S - 1; ++ci, ++i) issue(ci, i);
+      for (int64_t cj = ci; cj < c_end && cj % S != S - 1; ++cj) {
+        const int32_t row = int32_t((cj / S) * cap + (cj % S) * DA_KEYS);
+        tma_prefetch_l2_2d(&tmK, 0, row);
+        tma_prefetch_l2_2d(&tmV, 0, row);
+      }
+      griddep_wait();
+      for (; ci < c_end; ++ci, ++i) {
+        const int st = i % DA_NST;
+        if (!mbar_wait(&empty[st], ((i / DA_NST) & 1) ^ 1, status)) break;
+        issue(ci, st);
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  griddep_wait();   // q, the appended K / V rows and the counters are ready
+  const int g = lane >> 2, t = lane & 3, kw = warp * 32;
+  const uint32_t stage0 = smem_u32(stages);
+  uint32_t qa[4][2];
   float o[8][4];
+  float m_run = -INFINITY, l_run = 0.f;
+  int64_t cur_unit = -1;
+  int seg_first = 0;
+  for (int64_t ci = c_begin, i = 0; ci < c_end; ++ci, ++i) {
+    const int64_t unit = ci / S;
+    const int j = int(ci % S);
+    if (unit != cur_unit) {
+      // Q fragments: a0 = dims 16 ks + 2t, +1 and a2 = dims 16 ks + 8 + 2t, +1 of head g.
+      const bool live = g < G;
+      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+          q + ((unit / Hkv) * Hq + (unit % Hkv) * G + (live ? g : 0)) * DA_D);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;   // row g, log2 units
-
-  for (int kb = k0; kb < k1; kb += DA_BLOCK) {
-    const int nk = min(DA_BLOCK, k1 - kb);
-    // V block -> shared memory: row r (key), 16-byte chunk c stored at chunk c ^ (r & 7).
-    __syncwarp();
+      for (int ks = 0; ks < 4; ++ks) {
+        qa[ks][0] = live ? qrow[8 * ks + t] : 0u;
+        qa[ks][1] = live ? qrow[8 * ks + 4 + t] : 0u;
+      }
 #pragma unroll
-    for (int i = 0; i < (DA_BLOCK * 8) / 32; ++i) {
-      const int idx = i * 32 + lane, r = idx >> 3, c = idx & 7;
-      const int key = kb + min(r, nk - 1);
-      cp_async16(sv_addr + r * 128 + ((c ^ (r & 7)) << 4), vbase + int64_t(key) * DA_D + c * 8);
+      for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      m_run = -INFINITY;
+      l_run = 0.f;
+      cur_unit = unit;
+      seg_first = j;
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-
-    // S = Q K^T for 8 blocks of 8 keys; lane (g, t) loads key kb + 8 nb + g, dims 16t..16t+15.
-    float sacc[8][4];
+    const int st = int(i % DA_NST);
+    if (!mbar_wait(&full[st], uint32_t((i / DA_NST) & 1), status)) return;
+    const uint32_t kaddr = stage0 + st * DA_STAGE, vaddr = kaddr + DA_TILE;
+    const int nk = min(DA_KEYS, L - j * DA_KEYS);
+    const bool ragged = nk < kw + 32;
+    if (ragged) {
+      // Rows past the last key may hold anything (other units, unwritten cache slots):
+      // zero this warp's V rows there so that P = 0 never meets a NaN.
+      uint8_t* vt = stages + st * DA_STAGE + DA_TILE;
+      for (int idx = lane; idx < 32 * 8; idx += 32) {
+        const int r = kw + (idx >> 3);
+        if (r >= nk) reinterpret_cast<uint4*>(vt + r * 128)[idx & 7] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+    // S for the warp's 4 blocks of 8 keys.
+    float sacc[4][4];
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      const int key = kb + min(nb * 8 + g, nk - 1);
-      const uint4* kr = reinterpret_cast<const uint4*>(kbase + int64_t(key) * DA_D + 16 * t);
-      const uint4 lo = __ldg(kr), hi = __ldg(kr + 1);
-      const uint32_t kw[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    for (int nb = 0; nb < 4; ++nb) {
       sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
+      const int r = kw + nb * 8 + (lane & 7);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) mma_bf16_16816(sacc[nb], qa[ks], kw[2 * ks], kw[2 * ks + 1]);
+      for (int kp = 0; kp < 2; ++kp) {     // k-steps 2 kp and 2 kp + 1
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kaddr + sw128(r, 4 * kp + (lane >> 3)), b0, b1, b2, b3);
+        mma_bf16_16816(sacc[nb], qa[2 * kp][0], qa[2 * kp][1], b0, b1);
+        mma_bf16_16816(sacc[nb], qa[2 * kp + 1][0], qa[2 * kp + 1][1], b2, b3);
+      }
     }
-    // Online softmax on row g (columns 2t, 2t+1 of each 8-key block).
+    // Online softmax of row g (lane holds keys kw + 8 nb + 2t + e).
     float mx = -INFINITY;
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
+    for (int nb = 0; nb < 4; ++nb) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const bool ok = nb * 8 + 2 * t + e < nk;
+        const bool ok = kw + nb * 8 + 2 * t + e < nk;
         sacc[nb][e] = ok ? sacc[nb][e] * scale_log2 : -INFINITY;
         mx = fmaxf(mx, sacc[nb][e]);
       }
@@ -448,99 +504,136 @@ decode_attn_split_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float m_new = fmaxf(m_run, mx);
-    const float corr = ex2f(m_run - m_new);   // 0 on the first block (m_run = -inf)
+    const float mref = m_new == -INFINITY ? 0.f : m_new;   // nothing seen yet: all p = 0
+    const float corr = ex2f(m_run - mref);                  // 0 while m_run = -inf
     m_run = m_new;
     float psum = 0.f;
-    uint32_t pa[8];
+    uint32_t pa[4];
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      const float p0 = ex2f(sacc[nb][0] - m_new), p1 = ex2f(sacc[nb][1] - m_new);
+    for (int nb = 0; nb < 4; ++nb) {
+      const float p0 = ex2f(sacc[nb][0] - mref), p1 = ex2f(sacc[nb][1] - mref);
       psum += p0 + p1;
       pa[nb] = pack_bf16x2(p0, p1);
     }
-    l_run = l_run * corr + psum;
+    l_run = fmaf(l_run, corr, psum);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o[i][0] *= corr;
-      o[i][1] *= corr;
+    for (int n = 0; n < 8; ++n) {
+      o[n][0] *= corr;
+      o[n][1] *= corr;
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncwarp();
-    // O += P V: k-step kk covers keys 16 kk .. 16 kk + 15 (S blocks 2 kk and 2 kk + 1).
+    // O += P V over the warp's 32 keys (k-steps of 16), 8 blocks of 8 dims.
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t a[4] = {pa[2 * kk], 0u, pa[2 * kk + 1], 0u};
+    for (int kk = 0; kk < 2; ++kk) {
+      const int mi = lane >> 3, r = kw + 16 * kk + (mi & 1) * 8 + (lane & 7);
 #pragma unroll
-      for (int nb2 = 0; nb2 < 4; ++nb2) {   // dims 16 nb2 .. 16 nb2 + 15 (two n-blocks)
-        const int mi = lane >> 3, r = 16 * kk + (mi & 1) * 8 + (lane & 7);
-        const int c = 2 * nb2 + (mi >> 1);
+      for (int nb2 = 0; nb2 < 4; ++nb2) {
         uint32_t b0, b1, b2, b3;
-        ldsm_x4_trans(sv_addr + r * 128 + ((c ^ (r & 7)) << 4), b0, b1, b2, b3);
-        mma_bf16_16816(o[2 * nb2], a, b0, b1);
-        mma_bf16_16816(o[2 * nb2 + 1], a, b2, b3);
+        ldsm_x4_trans(vaddr + sw128(r, 2 * nb2 + (mi >> 1)), b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * nb2], pa[2 * kk], pa[2 * kk + 1], b0, b1);
+        mma_bf16_16816(o[2 * nb2 + 1], pa[2 * kk], pa[2 * kk + 1], b2, b3);
       }
     }
-  }
-  // Row sums: each lane holds 16 of the block's 64 columns per step.
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-  if (g < G) {
-    const int64_t base = (int64_t(bhk) * parts + part) * G + g;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      *reinterpret_cast<float2*>(opart + base * DA_D + 8 * i + 2 * t) = make_float2(o[i][0], o[i][1]);
-    if (t == 0) {
-      mlpart[base * 2] = m_run;
-      mlpart[base * 2 + 1] = l_run;
-    }
-  }
-}
+    // Release the stage (the zeroing writes were generic-proxy: order them before the
+    // next TMA write into the same bytes).
+    if (ragged) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
 
-// out[b, h*D + d] = sum_s 2^(m_s - M) o_s[d] / sum_s 2^(m_s - M) l_s  (bf16).
-// One CTA of 64 threads per (b, h): the first warp reduces the partials' maxima and sums
-// (lane s owns partial s, parts <= 64), the weights go to shared memory, then every
-// thread sums its dim over the partials with independent loads.
-__global__ void __launch_bounds__(DA_D)
-decode_attn_combine_kernel(const float* __restrict__ opart, const float* __restrict__ mlpart,
-                           __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int nparts) {
-  griddep_launch_dependents();
-  griddep_wait();
-  __shared__ float wgt[64];
-  __shared__ float inv_den;
-  const int G = Hq / Hkv;
-  const int bh = blockIdx.x;            // b * Hq + h
-  const int b = bh / Hq, h = bh % Hq;
-  const int bhk = b * Hkv + h / G, g = h % G;
-  const int tid = threadIdx.x;
-  if (tid < 32) {
-    float m[2], l[2];
+    if (ci + 1 != c_end && j + 1 != S) continue;
+    // ------------------------------------------------ end of this unit's segment
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    if (g < G) {
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int s = tid + 32 * k;
-      const int64_t i = (int64_t(bhk) * nparts + s) * G + g;
-      m[k] = s < nparts ? mlpart[i * 2] : -INFINITY;
-      l[k] = s < nparts ? mlpart[i * 2 + 1] : 0.f;
+      for (int n = 0; n < 8; ++n)
+        *reinterpret_cast<float2*>(s_o + (warp * 8 + g) * DA_D + 8 * n + 2 * t) =
+            make_float2(o[n][0], o[n][1]);
+      if (t == 0) {
+        s_m[warp][g] = m_run;
+        s_l[warp][g] = l_run;
+      }
     }
-    float M = fmaxf(m[0], m[1]);
+    consumers_sync();
+    const int64_t pbase = (unit * S + seg_first) * G;
+    for (int idx = threadIdx.x; idx < G * (DA_D / 4); idx += DA_WARPS * 32) {
+      const int gg = idx / (DA_D / 4), d = (idx % (DA_D / 4)) * 4;
+      float M = s_m[0][gg];                      // warp 0 always holds a valid key
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float den = 0.f;
+      for (int w = 1; w < DA_WARPS; ++w) M = fmaxf(M, s_m[w][gg]);
+      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+      float den = 0.f;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const float w = (m[k] == -INFINITY) ? 0.f : ex2f(m[k] - M);
-      wgt[tid + 32 * k] = w;
-      den = fmaf(w, l[k], den);
+      for (int w = 0; w < DA_WARPS; ++w) {
+        const float wt = s_m[w][gg] == -INFINITY ? 0.f : ex2f(s_m[w][gg] - M);
+        const float4 v = *reinterpret_cast<const float4*>(s_o + (w * 8 + gg) * DA_D + d);
+        num.x = fmaf(wt, v.x, num.x);
+        num.y = fmaf(wt, v.y, num.y);
+        num.z = fmaf(wt, v.z, num.z);
+        num.w = fmaf(wt, v.w, num.w);
+        den = fmaf(wt, s_l[w][gg], den);
+      }
+      *reinterpret_cast<float4*>(opart + (pbase + gg) * DA_D + d) = num;
+      if (d == 0) *reinterpret_cast<float2*>(mlpart + (pbase + gg) * 2) = make_float2(M, den);
     }
+    __threadfence();
+    consumers_sync();
+    if (threadIdx.x == 0) {
+      const uint32_t n = uint32_t(j - seg_first + 1);
+      s_last = atomicAdd(&counters[unit], n) + n == uint32_t(S) ? 1u : 0u;
+    }
+    consumers_sync();
+    if (s_last) {
+      // This CTA completed the unit.  Its partials sit in the slots of its segments' first
+      // chunks: chunk 0 of the unit and every CTA range start inside the unit.
+      __threadfence();
+      const int64_t u0 = unit * S, P = gridDim.x;
+      int64_t c0 = u0 * P / n_chunks;            // the CTA whose range holds chunk u0
+      while (c0 + 1 < P && n_chunks * (c0 + 1) / P <= u0) ++c0;
+      while (c0 > 0 && n_chunks * c0 / P > u0) --c0;
+      const int64_t b = unit / Hkv, kvh = unit % Hkv;
+      for (int idx = threadIdx.x; idx < G * (DA_D / 4); idx += DA_WARPS * 32) {
+        const int gg = idx / (DA_D / 4), d = (idx % (DA_D / 4)) * 4;
+        float M = -INFINITY, den = 0.f;
+        float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t c = c0; c < P; c += 4) {
+          // Up to 4 segments per batch, all loads in flight, then an online merge.
+          float2 ml[4];
+          float4 ov[4];
+          bool live[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    if (tid == 0) inv_den = den > 0.f ? 1.0f / den : 0.f;
+          for (int k = 0; k < 4; ++k) {
+            const int64_t start = c + k == c0 ? u0 : n_chunks * (c + k) / P;
+            live[k] = c + k < P && start < u0 + S && start >= u0;
+            const int64_t i = (live[k] ? start : u0) * G + gg;
+            ml[k] = __ldcg(reinterpret_cast<const float2*>(mlpart + i * 2));
+            ov[k] = __ldcg(reinterpret_cast<const float4*>(opart + i * DA_D + d));
+          }
+          float Mb = M;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) if (live[k]) Mb = fmaxf(Mb, ml[k].x);
+          const float corr = ex2f(M - Mb);        // 0 on the first batch (M = -inf)
+          num.x *= corr; num.y *= corr; num.z *= corr; num.w *= corr;
+          den *= corr;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (!live[k]) continue;
+            const float w = ex2f(ml[k].x - Mb);
+            num.x = fmaf(w, ov[k].x, num.x);
+            num.y = fmaf(w, ov[k].y, num.y);
+            num.z = fmaf(w, ov[k].z, num.z);
+            num.w = fmaf(w, ov[k].w, num.w);
+            den = fmaf(w, ml[k].y, den);
+          }
+          M = Mb;
+          if (!live[3]) break;
+        }
+        const float inv = 1.0f / den;
+        *reinterpret_cast<uint2*>(out + (b * Hq + kvh * G + gg) * DA_D + d) =
+            make_uint2(pack_bf16x2(num.x * inv, num.y * inv), pack_bf16x2(num.z * inv, num.w * inv));
+      }
+    }
+    consumers_sync();   // the merge area is free again
   }
-  __syncthreads();
-  const float* op = opart + (int64_t(bhk) * nparts * G + g) * DA_D + tid;
-  float num = 0.f;
-#pragma unroll 4
-  for (int s = 0; s < nparts; ++s) num = fmaf(wgt[s], __ldg(op + int64_t(s) * G * DA_D), num);
-  out[int64_t(bh) * DA_D + tid] = __float2bfloat16_rn(num * inv_den);
 }
 
 }  // namespace
@@ -583,8 +676,8 @@ int pick_splits(int64_t N, int64_t K, int sms) {
 }
 
 struct Layout {
-  size_t partial, xn, q, attn, h1, h1n, act, opart, mlpart, total;
-  int attn_splits, attn_chunk;
+  size_t partial, xn, q, attn, h1, h1n, act, opart, mlpart, counters, total;
+  int attn_splits;
 };
 
 Layout plan(const enigma_decode_layer_desc& d, int sms) {
@@ -595,14 +688,10 @@ Layout plan(const enigma_decode_layer_desc& d, int sms) {
   int64_t part = 0;
   for (auto& g : gemms) part = std::max(part, pick_splits(g[0], g[1], sms) * B * g[0]);
   Layout l;
-  // Split the keys so (sequence, kv head, chunk) CTAs cover ~4 per SM, at most 16 chunks
-  // (4 warp partials each; the combine kernel takes up to 64 partials).  The workspace is
-  // sized for that maximum, so one workspace serves every position.
-  const int64_t splits = std::min<int64_t>(
-      16, std::max<int64_t>(1, (4 * int64_t(sms) + B * Hkv - 1) / (B * Hkv)));
-  const int64_t chunk = (L + splits - 1) / splits;
-  l.attn_splits = int((L + chunk - 1) / chunk);
-  l.attn_chunk = int(chunk);
+  // Attention CTAs take 128-key chunks of one (sequence, kv head); the partial buffers
+  // are sized for the cache capacity, so one workspace serves every position.
+  const int64_t smax = (d.cache_capacity + DA_KEYS - 1) / DA_KEYS;
+  l.attn_splits = int((L + DA_KEYS - 1) / DA_KEYS);
   const int64_t G = Hq / Hkv;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align256(off + bytes); return o; };
@@ -613,8 +702,9 @@ Layout plan(const enigma_decode_layer_desc& d, int sms) {
   l.h1 = take(size_t(B * H) * 2);
   l.h1n = take(size_t(B * H) * 2);
   l.act = take(size_t(B * I) * 2);
-  l.opart = take(size_t(B * Hkv * splits * DA_WARPS * G * D) * 4);
-  l.mlpart = take(size_t(B * Hkv * splits * DA_WARPS * G * 2) * 4);
+  l.opart = take(size_t(B * Hkv * smax * G * D) * 4);
+  l.mlpart = take(size_t(B * Hkv * smax * G * 2) * 4);
+  l.counters = take(size_t(B * Hkv) * 4);
   l.total = off;
   return l;
 }
@@ -664,19 +754,26 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
                         static_cast<const float*>(part), sp, B, Nqkv, Hq, Hkv, d.rope_cos,
                         d.rope_sin, bfp(l.q), static_cast<__nv_bfloat16*>(d.k_cache),
                         static_cast<__nv_bfloat16*>(d.v_cache), int(d.cache_capacity),
-                        int(d.position)));
-  // 4-5. attention over position + 1 keys, split-KV then combine
-  ENIGMA_TRY(launch_pdl(decode_attn_split_kernel, dim3(B * Hkv, l.attn_splits),
-                        dim3(DA_WARPS * 32), 0, s, static_cast<const __nv_bfloat16*>(bfp(l.q)),
-                        static_cast<const __nv_bfloat16*>(d.k_cache),
-                        static_cast<const __nv_bfloat16*>(d.v_cache),
-                        reinterpret_cast<float*>(w + l.opart),
-                        reinterpret_cast<float*>(w + l.mlpart), Hq, Hkv, int(d.cache_capacity),
-                        int(d.position + 1), l.attn_chunk, d.attn_scale * 1.4426950408889634f));
-  ENIGMA_TRY(launch_pdl(decode_attn_combine_kernel, dim3(B * Hq), dim3(DA_D), 0, s,
-                        static_cast<const float*>(reinterpret_cast<float*>(w + l.opart)),
-                        static_cast<const float*>(reinterpret_cast<float*>(w + l.mlpart)),
-                        bfp(l.attn), Hq, Hkv, l.attn_splits * DA_WARPS));
+                        int(d.position), reinterpret_cast<uint32_t*>(w + l.counters)));
+  // 4. attention over position + 1 keys (split-KV, combined by each unit's last CTA)
+  {
+    CUtensorMap tk, tv;
+    const uint64_t rows = uint64_t(B) * Hkv * uint64_t(d.cache_capacity);
+    if (!make_tmap_bf16_2d(&tk, d.k_cache, rows, DA_D, DA_D, DA_D, DA_KEYS) ||
+        !make_tmap_bf16_2d(&tv, d.v_cache, rows, DA_D, DA_D, DA_D, DA_KEYS))
+      return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DA_SMEM);   // per device, cheap: set on every call
+    if (e != cudaSuccess) return e;
+    const int64_t chunks = int64_t(B) * Hkv * l.attn_splits;
+    const int ctas = int(std::min<int64_t>(chunks, int64_t(sms) * DA_CTAS_PER_SM));
+    ENIGMA_TRY(launch_pdl(decode_attn_kernel, dim3(ctas), dim3(DA_THREADS), DA_SMEM, s, tk, tv, static_cast<const __nv_bfloat16*>(bfp(l.q)),
+                          reinterpret_cast<float*>(w + l.opart),
+                          reinterpret_cast<float*>(w + l.mlpart),
+                          reinterpret_cast<uint32_t*>(w + l.counters), bfp(l.attn), Hq, Hkv,
+                          int(d.cache_capacity), int(d.position + 1), l.attn_splits, B * Hkv,
+                          d.attn_scale * 1.4426950408889634f, status));
+  }
   // 6-7. O projection + residual(x) -> h1, post-attention RMSNorm -> h1n
   sp = pick_splits(H, Hq * D, sms);
   ENIGMA_TRY(splitk_gemm(bfp(l.attn), d.w_o, part, B, H, Hq * D, sp, status, s));
