@@ -12,9 +12,9 @@
 //   * The split reduction is fused with what follows each GEMM: RoPE + KV-cache
 //     append (QKV), residual add + RMSNorm (O-proj), SwiGLU (gate/up), residual
 //     add (down-proj).
-//   * Attention is split-KV ("flash decoding"): CTAs of (sequence, kv head,
-//     key chunk) write (max, sum, o) partials for the group's query heads; a
-//     combine kernel merges the chunks.
+//   * Attention is split-KV ("flash decoding") in one persistent kernel: CTAs stream
+//     balanced ranges of (sequence x kv head, 128-key chunk) pairs through a TMA ring,
+//     and the CTA that finishes a (sequence, kv head) merges its partials.
 //
 // Workspace (caller-owned, enigma_decode_workspace_bytes) holds every partial
 // and intermediate, so a step makes no allocation.
