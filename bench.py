@@ -61,23 +61,58 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and throttle-reason sampling during the timed region (read-only).
+
+    The GPU is found by its UUID (the torch device index differs from the physical one
+    under CUDA_VISIBLE_DEVICES).  NVML is polled every 10 ms; without NVML, nvidia-smi
+    every 200 ms."""
 
     Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event-reason bits, in the order of Q's reason columns.
+    BITS = (0x8, 0x40, 0x20, 0x4)
 
     def __init__(self, index: int):
         self.index = index
+        self.uuid = None
+        try:
+            import torch
+            u = str(torch.cuda.get_device_properties(index).uuid)
+            self.uuid = u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            pass
         self.samples = []
         self._stop = threading.Event()
         self._t = None
 
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        if self.uuid:
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(self.uuid.encode())
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
     def _run(self):
+        try:
+            nv, h = self._nvml_handle()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self._stop.is_set():
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = reasons(h)
+                self.samples.append([str(sm), str(mx)] +
+                                    ["Active" if r & bit else "Not Active" for bit in self.BITS])
+                self._stop.wait(0.01)
+            return
+        except Exception:
+            pass
+        dev = self.uuid or str(self.index)
         while not self._stop.is_set():
             try:
                 out = subprocess.run(
-                    ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                    ["nvidia-smi", "-i", dev, f"--query-gpu={self.Q}",
                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5
                 ).stdout.strip()
                 if out:
