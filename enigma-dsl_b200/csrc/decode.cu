@@ -317,8 +317,8 @@ __device__ __forceinline__ float ex2f(float x) {
 // 128-key chunk) pairs; CTA c of P takes the contiguous range [c T / P, (c + 1) T / P),
 // so every SM streams the same number of chunks whatever the batch and head counts.
 //   * Warp 4 is the producer: one TMA box of K and one of V per chunk (128 rows x 128 B,
-//     128-byte swizzle) into a DA_NST-stage ring.  Chunks that do not hold the key
-//     appended by the predecessor are requested before the programmatic-launch wait.
+//     128-byte swizzle) into a DA_NST-stage ring.  The first chunks, if they do not hold
+//     the key appended by the predecessor, are requested before the programmatic wait.
 //   * Warps 0..3 each take 32 keys of every chunk:
 //       S = Q K^T  (Q = the group's G <= 8 heads as the 16-row A operand, rows >= G zero;
 //                  K from shared memory by ldmatrix),
@@ -412,16 +412,12 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         tma_load_2d(dst, &tmK, &full[st], 0, row);
         tma_load_2d(dst + DA_TILE, &tmV, &full[st], 0, row);
       };
-      // Before the wait: the first stages and an L2 prefetch of the rest of the range,
-      // stopping at the first chunk that holds an appended key (the last of a unit).
+      // Before the wait: the first stages, stopping at the first chunk that holds an
+      // appended key (the last of a unit).  (An L2 prefetch of the rest of the range was
+      // measured 1.7 us slower: it queues the ring's demand loads behind 67 MB of prefetch.)
       int64_t ci = c_begin;
       int i = 0;
       for (; ci < c_end && i < DA_NST && ci % S != S - 1; ++ci, ++i) issue(ci, i);
-      for (int64_t cj = ci; cj < c_end && cj % S != S - 1; ++cj) {
-        const int32_t row = int32_t((cj / S) * cap + (cj % S) * DA_KEYS);
-        tma_prefetch_l2_2d(&tmK, 0, row);
-        tma_prefetch_l2_2d(&tmV, 0, row);
-      }
       griddep_wait();
       for (; ci < c_end; ++ci, ++i) {
         const int st = i % DA_NST;
