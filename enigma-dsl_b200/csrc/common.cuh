@@ -31,7 +31,7 @@ cudaError_t sdpa_f32_launch(const void* Q, const void* K, const void* V, void* O
 cudaError_t sdpa_strided_launch(int dtype, const void* Q, const void* K, const void* V, void* O,
                                 int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv,
                                 int64_t D, const int64_t* strides12, float scale, bool causal,
-                                cudaStream_t s);
+                                const float* sinks, cudaStream_t s);
 cudaError_t sdpa_bf16_launch(const void* Q, const void* K, const void* V, void* O, int64_t B,
                              int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
                              float scale, bool causal, cudaStream_t s);

@@ -116,7 +116,8 @@ cudaError_t qwen_decode_f32_launch(const enigma_qwen_decode_f32_desc& q, cudaStr
   // Q [1, Hq, 1, D], K/V [1, Hkv, CT, D], O [1, Hq, 1, D].
   const int64_t st[12] = {0, D, D, 0, int64_t(CT) * D, D, 0, int64_t(CT) * D, D, 0, D, D};
   ENIGMA_TRY(sdpa_strided_launch(ENIGMA_DTYPE_F32, q.q_rope_buf, q.k_cache, q.v_cache,
-                                 q.attn_buf, 1, Hq, Hkv, 1, CT, D, st, q.attn_scale, false, s));
+                                 q.attn_buf, 1, Hq, Hkv, 1, CT, D, st, q.attn_scale, false,
+                                 nullptr, s));
   ENIGMA_TRY(gemv(q.Wo, q.attn_buf, q.x, q.norm_buf, H, QSZ));         // oproj (+ x)
   ENIGMA_TRY(rmsnorm_launch(ENIGMA_DTYPE_F32, q.norm_buf, q.w_post, q.post_buf, 1, H, q.eps, s));
   swiglu_gemv_f32_kernel<<<(I + 7) / 8, 256, 0, s>>>(q.Wg, q.Wu, q.post_buf, q.mlp_buf, I, H);

@@ -113,10 +113,11 @@ int32_t enigma_sdpa_f32(const void* Q, const void* K, const void* V, void* O, in
                        "sdpa_f32");
 }
 
-int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const void* V, void* O,
-                            int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
-                            int64_t seq_kv, int64_t head_dim, const int64_t* strides12,
-                            float scale, int32_t causal, void* stream) {
+int32_t enigma_sdpa_strided_sinks(int32_t dtype, const void* Q, const void* K, const void* V,
+                                  void* O, int64_t batch, int64_t heads_q, int64_t heads_kv,
+                                  int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                                  const int64_t* strides12, float scale, int32_t causal,
+                                  const float* sinks, void* stream) {
   if (dtype != ENIGMA_DTYPE_F32 && dtype != ENIGMA_DTYPE_BF16) return bad("sdpa: dtype");
   if (batch < 0 || heads_q <= 0 || heads_kv <= 0 || seq_q < 0 || seq_kv < 0 || head_dim <= 0)
     return bad("sdpa: sizes must be positive");
@@ -128,10 +129,19 @@ int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const v
   if (batch == 0 || seq_q == 0) return ENIGMA_OK;
   if (seq_kv == 0) return bad("sdpa: seq_kv must be > 0 when seq_q > 0");
   if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) return bad("sdpa: NULL buffer");
+  if (sinks != nullptr && !aligned(sinks, 4)) return bad("sdpa: sinks must be 4-byte aligned");
   return launch_status(enigma::sdpa_strided_launch(dtype, Q, K, V, O, batch, heads_q, heads_kv,
                                                    seq_q, seq_kv, head_dim, strides12, scale,
-                                                   causal != 0, as_stream(stream)),
+                                                   causal != 0, sinks, as_stream(stream)),
                        "sdpa_strided");
+}
+
+int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const void* V, void* O,
+                            int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
+                            int64_t seq_kv, int64_t head_dim, const int64_t* strides12,
+                            float scale, int32_t causal, void* stream) {
+  return enigma_sdpa_strided_sinks(dtype, Q, K, V, O, batch, heads_q, heads_kv, seq_q, seq_kv,
+                                   head_dim, strides12, scale, causal, nullptr, stream);
 }
 
 }  // extern "C"

@@ -34,7 +34,7 @@ template <typename T>
 __global__ void __launch_bounds__(128)
 sdpa_simt_kernel(const T* __restrict__ Q, const T* __restrict__ K, const T* __restrict__ V,
                  T* __restrict__ O, int64_t B, int Hq, int Hkv, int64_t Sq, int64_t Skv, int D,
-                 float scale, int causal, Strides st) {
+                 float scale, int causal, Strides st, const float* __restrict__ sinks) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * 4 + warp;  // over B*Hq*Sq
   const int64_t total = B * Hq * Sq;
@@ -78,6 +78,16 @@ sdpa_simt_kernel(const T* __restrict__ Q, const T* __restrict__ K, const T* __re
     }
     m = m_new;
   }
+  // An attention sink (gpt-oss; examples/metal/sdpa_handwritten.metal:39-42 start the
+  // running max at s[h] with l = 1) adds exp(s_h - M) to the denominator only.
+  if (sinks != nullptr) {
+    const float sk = sinks[h];
+    const float m_new = fmaxf(m, sk);
+    const float corr = expf(m - m_new);
+    l = l * corr + expf(sk - m_new);
+#pragma unroll
+    for (int t = 0; t < kMaxDPerLane; ++t) acc[t] *= corr;
+  }
   // last < 0 only when causal with Sq > Skv: the row sees no key; it is defined as 0.
   const float inv = l > 0.f ? 1.0f / l : 0.f;
 #pragma unroll
@@ -101,13 +111,13 @@ Strides dense_strides(int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t 
 template <typename T>
 cudaError_t launch(const void* Q, const void* K, const void* V, void* O, int64_t B, int64_t Hq,
                    int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, float scale, bool causal,
-                   cudaStream_t s, const Strides& st) {
+                   cudaStream_t s, const Strides& st, const float* sinks = nullptr) {
   const int64_t rows = B * Hq * Sq;
   const int64_t blocks = (rows + 3) / 4;
   if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
   sdpa_simt_kernel<T><<<unsigned(blocks), 128, 0, s>>>(
       static_cast<const T*>(Q), static_cast<const T*>(K), static_cast<const T*>(V),
-      static_cast<T*>(O), B, int(Hq), int(Hkv), Sq, Skv, int(D), scale, causal ? 1 : 0, st);
+      static_cast<T*>(O), B, int(Hq), int(Hkv), Sq, Skv, int(D), scale, causal ? 1 : 0, st, sinks);
   return cudaGetLastError();
 }
 
@@ -130,7 +140,7 @@ cudaError_t sdpa_f32_launch(const void* Q, const void* K, const void* V, void* O
 cudaError_t sdpa_strided_launch(int dtype, const void* Q, const void* K, const void* V, void* O,
                                 int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv,
                                 int64_t D, const int64_t* strides12, float scale, bool causal,
-                                cudaStream_t s) {
+                                const float* sinks, cudaStream_t s) {
   Strides st;
   for (int i = 0; i < 3; ++i) {
     st.q[i] = strides12[i];
@@ -139,7 +149,7 @@ cudaError_t sdpa_strided_launch(int dtype, const void* Q, const void* K, const v
     st.o[i] = strides12[9 + i];
   }
   if (dtype == ENIGMA_DTYPE_F32)
-    return launch<float>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, D, scale, causal, s, st);
-  return launch<__nv_bfloat16>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, D, scale, causal, s, st);
+    return launch<float>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, D, scale, causal, s, st, sinks);
+  return launch<__nv_bfloat16>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, D, scale, causal, s, st, sinks);
 }
 }  // namespace enigma

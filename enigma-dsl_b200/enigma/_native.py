@@ -57,6 +57,8 @@ PROTOTYPES = {
     "enigma_sdpa_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp],
     "enigma_sdpa_strided": [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                             _c.POINTER(_i64), _f32, _i32, _vp],
+    "enigma_sdpa_strided_sinks": [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                  _i64, _c.POINTER(_i64), _f32, _i32, _vp, _vp],
     "enigma_decode_workspace_bytes": [_vp, _c.POINTER(_sz)],
     "enigma_decode_layer_bf16": [_vp, _vp, _vp, _vp, _sz, _vp],
     "enigma_qwen_decode_f32": [_vp, _vp],

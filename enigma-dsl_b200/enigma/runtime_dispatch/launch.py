@@ -114,13 +114,38 @@ def _plan_gemm(b, nbytes):
 
 
 def _plan_sdpa(b, nbytes, grid, threads):
-    _need(len(nbytes) == 4, f"attention binds 4 buffers, got {len(nbytes)}")
     es, dt = _ES[b.dtype], _DT[b.dtype]
     scale = float(b.params.get("scale", 1.0))
     causal = int(bool(b.params.get("causal", False)))
+    if b.layout == "gptoss_args":
+        # The hand-written gpt-oss kernel: buffers args, q [tokens, qkv_dim], kv per kv head
+        # (kv_stride elements: [token, K|V]), s (Hq sink logits), o [tokens, Hq * D].
+        _need(len(nbytes) == 5, f"sdpa_gptoss binds 5 buffers (args, q, kv, s, o), got {len(nbytes)}")
+        d, hq, qmul = (int(b.params[k]) for k in ("head_dim", "num_q_heads", "qmul"))
+        hkv = int(grid[1])
+        tokens = int(grid[0]) // max(1, int(threads[0]))
+        _need(hkv * qmul == hq, f"grid.y = {hkv} kv heads x qmul {qmul} != {hq} query heads")
+        qkv_dim, kv_tokens, kv_stride = (int(b.params[k]) for k in ("qkv_dim", "kv_tokens",
+                                                                     "kv_stride"))
+        _need(nbytes[1] >= ((tokens - 1) * qkv_dim + hq * d) * 4, "sdpa_gptoss: q buffer too small")
+        _need(nbytes[2] >= ((hkv - 1) * kv_stride + kv_tokens * 2 * d) * 4,
+              "sdpa_gptoss: kv buffer too small for args.kv_stride / num_kv_tokens")
+        _need(nbytes[3] >= hq * 4 and nbytes[4] >= tokens * hq * d * 4,
+              "sdpa_gptoss: s / output buffer too small")
+        strides = (ctypes.c_int64 * 12)(0, d, qkv_dim, 0, kv_stride, 2 * d, 0, kv_stride, 2 * d,
+                                        0, d, hq * d)
+
+        def fn(p, stream):
+            _native.call("enigma_sdpa_strided_sinks", dt, p[1], p[2], p[2] + d * es, p[4], 1, hq,
+                         hkv, tokens, kv_tokens, d, strides, ctypes.c_float(scale), causal, p[3],
+                         stream)
+        return LaunchPlan(f"sdpa_gptoss tokens={tokens} Hq={hq} Hkv={hkv} D={d} "
+                          f"kv_tokens={kv_tokens}", fn, (4,))
+    _need(len(nbytes) == 4, f"attention binds 4 buffers, got {len(nbytes)}")
     if b.layout == "gqa_interleaved":
-        # Q, O: [tokens, Hq, D]; KV: [Hkv, kv_tokens, 2D] (K then V); buffer 2: Hq floats
-        # (the running max start value, -1e30 in the example, so it never binds).
+        # Q, O: [tokens, Hq, D]; KV: [Hkv, kv_tokens, 2D] (K then V); buffer 2: Hq floats,
+        # the sink logit each head's running max starts from (with l = 1 on the first
+        # simdgroup, benchmark_sdpa.py:64-72); -1e30 in the example, where it adds nothing.
         hq = _div(nbytes[2], 4, "running-max buffer")
         hkv = int(grid[1])
         tokens = int(grid[0]) // int(threads[0])
@@ -132,8 +157,9 @@ def _plan_sdpa(b, nbytes, grid, threads):
                                         0, kv_tokens * 2 * d, 2 * d, 0, d, hq * d)
 
         def fn(p, stream):
-            _native.call("enigma_sdpa_strided", dt, p[0], p[1], p[1] + d * es, p[3], 1, hq, hkv,
-                         tokens, kv_tokens, d, strides, ctypes.c_float(scale), causal, stream)
+            _native.call("enigma_sdpa_strided_sinks", dt, p[0], p[1], p[1] + d * es, p[3], 1, hq,
+                         hkv, tokens, kv_tokens, d, strides, ctypes.c_float(scale), causal, p[2],
+                         stream)
         return LaunchPlan(f"sdpa gqa tokens={tokens} Hq={hq} Hkv={hkv} D={d} "
                           f"kv_tokens={kv_tokens}", fn, (3,))
     d = int(b.params["head_dim"])

@@ -28,6 +28,7 @@ import numpy as np
 
 from .. import _native
 from ..compiler.compiler import CompiledKernel
+from . import handwritten as _handwritten
 from . import launch as _launch
 
 _SCALAR_NP = {
@@ -164,8 +165,12 @@ class MetalRuntime:
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
-    def _binding(compiled: CompiledKernel):
+    def _binding(compiled: CompiledKernel, inputs=()):
         b = getattr(compiled, "cuda_kernel", None)
+        if b is None:
+            # A bare CompiledKernel around one of the reference's hand-written Metal kernels.
+            b = _handwritten.bind(compiled.kernel_name, getattr(compiled, "metal_source", ""),
+                                  list(inputs))
         if b is None:
             raise _gpu_error("compiled kernel has no sm_100a binding (was it built by "
                              "enigma.compile?)", kernel=compiled.kernel_name)
@@ -214,7 +219,7 @@ class MetalRuntime:
                 constants: Optional[dict] = None, output_shapes: Optional[List[tuple]] = None,
                 output_dtypes: Optional[List] = None):
         """One shot: bind (copying host inputs), launch, wait, read back, free."""
-        binding = self._binding(compiled)
+        binding = self._binding(compiled, inputs)
         torch_out = output_shapes is not None
         if torch_out:
             if output_dtypes is None or len(output_dtypes) != len(output_shapes):
@@ -282,7 +287,7 @@ class MetalRuntime:
     def prepare(self, compiled: CompiledKernel, inputs: List[Any], output_size: int
                 ) -> "PreparedKernel":
         """Bind once (inputs copied to the device) for repeated dispatch."""
-        binding = self._binding(compiled)
+        binding = self._binding(compiled, inputs)
         n_sc = len(getattr(compiled, "scalar_params", None) or [])
         num = getattr(compiled, "num_params", None)
         if num is not None and len(inputs) + n_sc + 1 != num:

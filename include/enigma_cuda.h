@@ -125,6 +125,16 @@ int32_t enigma_sdpa_strided(int32_t dtype, const void* Q, const void* K, const v
                             int64_t batch, int64_t heads_q, int64_t heads_kv, int64_t seq_q,
                             int64_t seq_kv, int64_t head_dim, const int64_t* strides12,
                             float scale, int32_t causal, void* stream);
+/* As enigma_sdpa_strided with an attention sink per query head (gpt-oss): sinks[h] is a
+ * logit in the same units as scale * q.k that joins the softmax denominator only, i.e.
+ * O = sum_j e^(s_j - M) v_j / (e^(sinks[h] - M) + sum_j e^(s_j - M)).  Replaces the
+ * sink / running-max buffer `s` of examples/metal/sdpa_handwritten.metal:16-42 (m starts at
+ * s[h], l at 1) and of sdpa_enigma (examples/benchmark_sdpa.py:64-72).  sinks may be NULL. */
+int32_t enigma_sdpa_strided_sinks(int32_t dtype, const void* Q, const void* K, const void* V,
+                                  void* O, int64_t batch, int64_t heads_q, int64_t heads_kv,
+                                  int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                                  const int64_t* strides12, float scale, int32_t causal,
+                                  const float* sinks, void* stream);
 
 /* ---- one decoder-layer decode step (Qwen-style; the reference's qwen_fused megakernel,
  *      examples/qwen_megakernel.py:228-269, at BASELINE config 5 shapes) ----

@@ -68,12 +68,15 @@ def gemm(a: np.ndarray, b: np.ndarray, c: np.ndarray | None = None) -> np.ndarra
 
 
 # --------------------------------------------------------------------------- SDPA
-def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float, causal: bool = False
-         ) -> np.ndarray:
+def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float, causal: bool = False,
+         sinks: np.ndarray | None = None) -> np.ndarray:
     """softmax(scale * Q K^T [+ mask]) V for [B, Hq, Sq, D] / [B, Hkv, Sk, D] inputs.
 
     Max-subtracted softmax as in showcase_attention.py:150-153; q-head h reads
-    kv-head h // (Hq // Hkv) as in benchmark_sdpa.py:198-208.  fp64 internally.
+    kv-head h // (Hq // Hkv) as in benchmark_sdpa.py:198-208.  `sinks` [Hq] (optional)
+    are attention-sink logits in the units of scale * q.k that join the denominator only
+    (the running max starts at s[h] with l = 1: examples/metal/sdpa_handwritten.metal:39-42,
+    benchmark_sdpa.py:64-72).  fp64 internally.
     """
     q = np.asarray(q, dtype=np.float64)
     k = np.asarray(k, dtype=np.float64)
@@ -93,9 +96,13 @@ def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float, causal: bool
             if mask is not None:
                 s = np.where(mask, -np.inf, s)
             m = np.max(s, axis=-1, keepdims=True)
+            if sinks is not None:
+                m = np.maximum(m, float(sinks[h]))
             m = np.where(np.isfinite(m), m, 0.0)
             p = np.exp(s - m)
             den = p.sum(axis=-1, keepdims=True)
+            if sinks is not None:
+                den = den + np.exp(float(sinks[h]) - m)
             out[b, h] = np.where(den > 0, (p @ v[b, h // g]) / np.where(den > 0, den, 1.0), 0.0)
     return out.astype(np.float32)
 

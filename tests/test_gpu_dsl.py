@@ -192,3 +192,24 @@ def test_rmsnorm_runtime_eps(rt, mode):
                      **kw)
     np.testing.assert_allclose(np.frombuffer(raw, np.float32).reshape(64, 1024),
                                orc.rmsnorm(x, w, 1e-2), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("sink", ["none", "finite"])
+def test_sdpa_gqa_sinks(rt, sink):
+    """The DSL gpt-oss kernel's buffer 2 is an attention sink (benchmark_sdpa.py:64-72): with
+    finite values it joins the softmax denominator."""
+    T, H, G, D, S = 16, 64, 8, 64, 100
+    jit, args, thr = K.make_sdpa_gqa(T, H, G, D, S)
+    ck = enigma.compile(jit, *args)
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((T, H, D)).astype(np.float32) * 0.3
+    k = rng.standard_normal((G, S, D)).astype(np.float32) * 0.3
+    v = rng.standard_normal((G, S, D)).astype(np.float32)
+    kv = np.concatenate([k, v], axis=2)
+    s0 = (np.full(H, -1e30) if sink == "none" else rng.standard_normal(H) * 2).astype(np.float32)
+    raw = rt.execute(ck, [q.ravel(), kv.ravel(), s0], T * H * D * 4, grid=ck.grid,
+                     threads=ck.block)
+    o = np.frombuffer(raw, np.float32).reshape(T, H, D)
+    ref = orc.sdpa(q.transpose(1, 0, 2)[None], k[None], v[None], 1.0,
+                   sinks=None if sink == "none" else s0)[0].transpose(1, 0, 2)
+    np.testing.assert_allclose(o, ref, rtol=1e-4, atol=1e-5)
