@@ -311,6 +311,76 @@ def _sdpa_tc_available() -> bool:
     return hasattr(_native.lib(), "enigma_sdpa_bf16")
 
 
+def _rmsnorm_line(rows, hidden, dtype, steps, warmup, stream, hbm_peak):
+    """One RMSNorm configuration (BASELINE configs 1 and 2): HBM GB/s of one read of x and
+    one write of y (+ w), L2 flushed by a read before every step (small sizes fit in L2)."""
+    import torch
+    from enigma import cuda_ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    x = torch.randn(rows, hidden, device="cuda", generator=g).to(tdt)
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).to(tdt)
+    y = torch.empty_like(x)
+    fn = lambda: cuda_ops.rmsnorm(x, w, EPS, out=y)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    ms = _time_device_flushed(fn, steps, stream)
+    es = x.element_size()
+    byts = 2 * rows * hidden * es + hidden * es
+    gbs = byts / (ms * 1e-3) / 1e9
+    return {"op": "rmsnorm", "dtype": dtype, "rows": rows, "hidden": hidden, "ms": round(ms, 4),
+            "value": round(gbs, 1), "unit": "GB/s", "frac_hbm": round(gbs / hbm_peak, 4),
+            "timing": "L2 flushed (256 MB read) before every step"}
+
+
+def run_sweep(args):
+    """Every BASELINE configuration on one GPU, one JSON line each (the headline and its
+    contract fields are the default run's; these lines are the per-config table)."""
+    import torch
+    from enigma import cuda_ops
+    cuda_ops.ensure_device(0)
+    stream = torch.cuda.current_stream()
+    hbm_peak, tc_peak, _ = _peaks()
+    steps, warm = max(5, min(args.steps, 30)), max(3, args.warmup)
+    print(json.dumps(_rmsnorm_line(4096, 4096, "f32", steps, warm, stream, hbm_peak) |
+                     {"config": 1}), flush=True)
+    for rows in (16384, 65536, 262144):
+        for hidden in (2048, 4096, 8192):
+            print(json.dumps(_rmsnorm_line(rows, hidden, "bf16", steps, warm, stream, hbm_peak) |
+                             {"config": 2}), flush=True)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for n in (1024, 4096, 8192):
+        a = (torch.randn(n, n, device="cuda", generator=g) / math.sqrt(n)).bfloat16()
+        b = torch.randn(n, n, device="cuda", generator=g).bfloat16()
+        c = torch.empty_like(a)
+        fn = lambda: cuda_ops.gemm(a, b, out=c)  # noqa: E731
+        for _ in range(warm):
+            fn()
+        ms = _time_device(fn, steps, stream)
+        tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
+        print(json.dumps({"config": 3, "op": "gemm_bf16", "n": n, "ms": round(ms, 4),
+                          "value": round(tf, 1), "unit": "TFLOP/s",
+                          "frac_tensor": round(tf / tc_peak, 4), "timing": "back to back"}),
+              flush=True)
+        del a, b, c
+    for S in (1024, 4096, 8192):
+        B, H, D = 8, 32, 128
+        q, k, v = (torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16() for _ in range(3))
+        o = torch.empty_like(q)
+        for causal in (True, False):
+            fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
+            for _ in range(warm):
+                fn()
+            ms = _time_device(fn, steps, stream)
+            tf = (2 if causal else 4) * B * H * S * S * D / (ms * 1e-3) / 1e12
+            print(json.dumps({"config": 4, "op": "sdpa_bf16", "S": S, "causal": causal,
+                              "ms": round(ms, 4), "value": round(tf, 1), "unit": "TFLOP/s",
+                              "frac_tensor": round(tf / tc_peak, 4), "timing": "back to back",
+                              "flops": "causal 2BHS^2D, non-causal 4BHS^2D"}), flush=True)
+        del q, k, v, o
+    print(json.dumps({"config": 5, "op": "decode_layer"} | _decode_side(hbm_peak)), flush=True)
+
+
 def run_ours(args):
     import torch
     from enigma import _native, cuda_ops
@@ -447,6 +517,11 @@ def run_single_op(args):
                           "gbs": round((layer.weight_bytes() + 2 * 64 * 2 * 2049 * 64 * 2)
                                        / (ms * 1e-3) / 1e9, 1)}), flush=True)
         return
+    if args.only == "rmsnorm":
+        hbm_peak = _peaks()[0]
+        print(json.dumps(_rmsnorm_line(args.rows, args.hidden, args.dtype, args.steps,
+                                       args.warmup, stream, hbm_peak)), flush=True)
+        return
     if args.only == "gemm":
         a = (torch.randn(n, n, device="cuda", generator=g) / math.sqrt(n)).bfloat16()
         b = torch.randn(n, n, device="cuda", generator=g).bfloat16()
@@ -479,14 +554,22 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=16384)
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (smaller cases are for profiling only)")
-    ap.add_argument("--only", choices=["gemm", "sdpa", "sdpa_causal", "decode"], default=None,
+    ap.add_argument("--only", choices=["gemm", "sdpa", "sdpa_causal", "decode", "rmsnorm"],
+                    default=None,
                     help="time one operator alone (profiling case)")
     ap.add_argument("--graph", action="store_true", help="--only decode: replay a CUDA graph")
     ap.add_argument("--size", type=int, default=4096, help="--only: n for GEMM n^3, S for SDPA")
+    ap.add_argument("--hidden", type=int, default=HIDDEN, help="--only rmsnorm: row width")
+    ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16", help="--only rmsnorm")
+    ap.add_argument("--sweep", action="store_true",
+                    help="every BASELINE configuration on one GPU, one JSON line each")
     args = ap.parse_args()
     _set_rows(args.rows)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.only:
         run_single_op(args)
         return
