@@ -358,10 +358,18 @@ def run_sweep(args):
             fn()
         ms = _time_device(fn, steps, stream)
         tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
+        # cuBLAS (torch.matmul) timed the same way, for a like-for-like reference under the
+        # same clocks and power state (a comparison line, not the product path).
+        ref = lambda: torch.matmul(a, b, out=c)  # noqa: E731
+        for _ in range(warm):
+            ref()
+        ms_ref = _time_device(ref, steps, stream)
+        tf_ref = 2 * n ** 3 / (ms_ref * 1e-3) / 1e12
         print(json.dumps({"config": 3, "op": "gemm_bf16", "n": n, "ms": round(ms, 4),
                           "value": round(tf, 1), "unit": "TFLOP/s",
-                          "frac_tensor": round(tf / tc_peak, 4), "timing": "back to back"}),
-              flush=True)
+                          "frac_tensor": round(tf / tc_peak, 4), "timing": "back to back",
+                          "cublas_same_loop_tflops": round(tf_ref, 1),
+                          "vs_cublas_same_loop": round(tf / tf_ref, 4)}), flush=True)
         del a, b, c
     for S in (1024, 4096, 8192):
         B, H, D = 8, 32, 128
