@@ -236,6 +236,10 @@ constexpr int P_B_BYTES = BK * (P_BN / 2) * 2;         // 16 KB: this CTA's 128 
 constexpr int P_STAGE = P_A_BYTES + P_B_BYTES;
 constexpr int P_SMEM = P_STAGES * P_STAGE + 1024 + 256;
 
+// HALF: every 256 x 256 tile runs as two 256 x 128 halves (MMA N = 128, one 64-column B box
+// per CTA), for problems with fewer tiles than CTA pairs: twice the pairs get work (1024^3:
+// 16 tiles -> 32 halves on 32 pairs).  The full-tile instance is used otherwise.
+template <bool HALF>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB, __nv_bfloat16* __restrict__ C,
@@ -279,7 +283,9 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   const uint32_t tmem_base = *tmem_slot;
 
   const TileSched sched{(M + P_BM - 1) / P_BM, (N + P_BN - 1) / P_BN};
-  const int num_tiles = sched.num_m * sched.num_n;
+  constexpr int UW = HALF ? P_BN / 2 : P_BN;            // unit width (columns)
+  constexpr int BOXES = UW / 128;                        // 64-column B boxes per CTA
+  const int num_tiles = sched.num_m * sched.num_n * (HALF ? 2 : 1);   // work units
   const int num_kb = (K + BK - 1) / BK;
   const int pair_id = int(blockIdx.x) >> 1, num_pairs = int(gridDim.x) >> 1;
 
@@ -292,16 +298,17 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       bool ok = true;
       for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
         int mb, nb;
-        sched.coords(t, mb, nb);
+        sched.coords(HALF ? t >> 1 : t, mb, nb);
+        const int n0 = nb * P_BN + (HALF ? (t & 1) * UW : 0);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status)) { ok = false; break; }
           const uint32_t fb = full_leader0 + stage * 8;
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (P_A_BYTES + BOXES * B_BOX_BYTES));
           tma_load_2d_pair(sA + stage * P_A_BYTES, &tmA, fb, kb * BK, mb * P_BM + int(rank) * 128);
           uint8_t* b = sB + stage * P_B_BYTES;
 #pragma unroll
-          for (int j = 0; j < 2; ++j)
-            tma_load_2d_pair(b + j * B_BOX_BYTES, &tmB, fb, nb * P_BN + int(rank) * 128 + j * 64,
+          for (int j = 0; j < BOXES; ++j)
+            tma_load_2d_pair(b + j * B_BOX_BYTES, &tmB, fb, n0 + int(rank) * (UW / 2) + j * 64,
                              kb * BK);
           if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
         }
@@ -311,7 +318,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader only)
     if (rank == 0 && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, P_BN, /*a_mn=*/false, /*b_mn=*/true);
+      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, UW, /*a_mn=*/false, /*b_mn=*/true);
       const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
       const uint32_t empty0_self = smem_u32(&empty[0]), empty0_peer = mapa_shared(empty0_self, peer);
       const uint32_t accf0_self = smem_u32(&acc_full[0]), accf0_peer = mapa_shared(accf0_self, peer);
@@ -353,15 +360,15 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     uint32_t acc_phase = 0;
     for (int t = pair_id; t < num_tiles; t += num_pairs) {
       int mb, nb;
-      sched.coords(t, mb, nb);
+      sched.coords(HALF ? t >> 1 : t, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, status)) break;
       tc_fence_after();
       const int row = mb * P_BM + row_in_tile;
-      const int col0 = nb * P_BN;
+      const int col0 = nb * P_BN + (HALF ? (t & 1) * UW : 0);
       __nv_bfloat16* crow = C + int64_t(row) * N;
       const uint32_t taddr = tmem_base + acc * P_BN + (uint32_t(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < P_BN; c += 32) {
+      for (int c = 0; c < UW; c += 32) {
         uint32_t r0[16], r1[16];
         tmem_ld16(taddr + c, r0);
         tmem_ld16(taddr + c + 16, r1);
@@ -474,13 +481,14 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
     if (e != cudaSuccess) return e;
     if (M >= 256 && N >= 256 && !(getenv("ENIGMA_GEMM_1SM") && getenv("ENIGMA_GEMM_1SM")[0] == '1')) {
       // CTA-pair kernel: B boxes of the pair's two N halves, A boxes of 128 rows.
-      e = cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               P_SMEM);
-      if (e != cudaSuccess) return e;
       const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
-      const int pairs = int(std::min<int64_t>(ptiles, sm_count() / 2));
-      gemm_bf16_pair_kernel<<<2 * pairs, THREADS, P_SMEM, s>>>(
-          ta, tb, static_cast<__nv_bfloat16*>(C), int(M), int(N), int(K), device_status());
+      const bool half = 2 * ptiles <= sm_count() / 2;
+      auto kern = half ? gemm_bf16_pair_kernel<true> : gemm_bf16_pair_kernel<false>;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+      if (e != cudaSuccess) return e;
+      const int pairs = int(std::min<int64_t>(half ? 2 * ptiles : ptiles, sm_count() / 2));
+      kern<<<2 * pairs, THREADS, P_SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), int(M),
+                                              int(N), int(K), device_status());
       return cudaGetLastError();
     }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);

@@ -72,7 +72,8 @@ def _check_bf16(got, ref):
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 256), (1024, 1024, 1024),
                                    (200, 136, 72), (1, 8, 8), (300, 264, 1000), (128, 256, 8),
-                                   (64, 64, 4), (33, 17, 5)])
+                                   (64, 64, 4), (33, 17, 5),
+                                   (2560, 2304, 256)])   # 90 tiles on 74 pairs: split tail
 def test_gemm_bf16(cuda, m, n, k):
     import torch
     from enigma import cuda_ops
