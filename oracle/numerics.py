@@ -119,6 +119,25 @@ def sdpa_rows(q, k, v, scale, causal, rows):
     return np.stack(res)
 
 
+def sdpa_query_rows(q_rows, k, v, scale, causal, row_idx, sk_minus_sq=0):
+    """Exact attention output for selected query rows of one (batch, head).
+
+    q_rows [R, D] are the queries at absolute positions row_idx [R]; k / v [Sk, D] the
+    head's keys and values.  Causal masking keeps key j for query i iff j <= i + (Sk - Sq),
+    as `sdpa`; the same max-subtracted softmax in fp64.  For full-size checks, where the
+    whole score matrix would not fit in host memory."""
+    q = np.asarray(q_rows, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    s = (q @ k.T) * scale
+    if causal:
+        j = np.arange(k.shape[0])[None, :]
+        s = np.where(j > np.asarray(row_idx)[:, None] + sk_minus_sq, -np.inf, s)
+    m = s.max(axis=1, keepdims=True)
+    p = np.exp(s - m)
+    return ((p @ v) / p.sum(axis=1, keepdims=True)).astype(np.float32)
+
+
 # --------------------------------------------------------------------------- error metrics
 def max_abs(a, b) -> float:
     return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))))
