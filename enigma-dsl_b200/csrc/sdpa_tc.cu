@@ -21,14 +21,14 @@
 //               every earlier MMA of the issuing thread, "S_i(j) done" also means
 //               "PV_i(j-1) done": the softmax may touch O_i after that wait.
 //   warps 2-5   softmax of Q0, warps 6-9 softmax of Q1; one thread per row:
-//               tcgen05.ld the S row, row max (3-input max), p = 2^(s*c - m*c)
-//               with packed f32x2 FMAs, row sum, P packed to bf16 and stored with
-//               tcgen05.st over the first half of S's columns.  About 3/8 of the
-//               exponentials run on the FMA pipe (Cody-Waite range reduction and a
-//               degree-4 polynomial, relative error 3.1e-6, fitted by least squares
-//               on Chebyshev nodes) so the MUFU unit is not the bottleneck.  O is
-//               rescaled only when a row max grows by more than 2^8 (exact: the
-//               numerator and denominator share the stale max).
+//               tcgen05.ld the S row, row max (3-input max), s*c - m*c with packed
+//               f32x2 FMAs, p = 2^() two at a time with the bf16x2 MUFU exponential
+//               (P is the bf16 operand of the PV MMA: no separate pack), row sum in
+//               fp32 of those bf16 values, P stored with tcgen05.st over the first
+//               half of S's columns.  The softmax is issue-bound, so instructions per
+//               score are what counts.  O is rescaled only when a row max grows by
+//               more than 2^8 (exact: the numerator and denominator share the stale
+//               max).
 // All mbarrier waits are bounded (sm100.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -104,24 +104,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x for a pair, on the FMA pipe, for softmax arguments x <= 0.  x < -125 gives 0
-// (so masked -inf entries contribute exactly nothing); otherwise x = n + f with
-// n = round(x) (the 1.5 * 2^23 shifter), f in [-0.5, 0.5], 2^f by a degree-4
-// polynomial and n added to the exponent field (the result stays a normal float).
-__device__ __forceinline__ float2 ex2_poly2(float2 x0) {
-  float2 x = make_float2(fmaxf(x0.x, -125.f), fmaxf(x0.y, -125.f));
-  const float2 shifter = make_float2(12582912.f, 12582912.f);
-  const float2 t = f2add(x, shifter);                       // round to integer in the mantissa
-  const float2 n = f2add(t, make_float2(-12582912.f, -12582912.f));
-  const float2 f = f2add(x, make_float2(-n.x, -n.y));
-  float2 p = make_float2(0.00960039533674717f, 0.00960039533674717f);
-  p = f2fma(p, f, make_float2(0.05591689422726631f, 0.05591689422726631f));
-  p = f2fma(p, f, make_float2(0.24023719131946564f, 0.24023719131946564f));
-  p = f2fma(p, f, make_float2(0.6931219696998596f, 0.6931219696998596f));
-  p = f2fma(p, f, make_float2(1.0f, 1.0f));
-  const int ex = __float_as_int(t.x) << 23, ey = __float_as_int(t.y) << 23;
-  return make_float2(x0.x < -125.f ? 0.f : __int_as_float(__float_as_int(p.x) + ex),
-                     x0.y < -125.f ? 0.f : __int_as_float(__float_as_int(p.y) + ey));
+// Two exponentials 2^x on the MUFU pipe in one bf16x2 operation: arguments and results
+// packed as bf16 pairs (the P operand of the PV MMA is bf16 anyway).  Half the MUFU
+// operations and no separate pack of P; the argument is rounded to bf16 first.
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 template <int D>
@@ -350,31 +339,25 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const float2 cc = make_float2(c, c), nmc = make_float2(-mc, -mc);
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};    // four independent accumulation chains
-      // exp, row sum, P store; with POLY, 3 of every 8 pairs run on the FMA pipe.
-      auto exp_store = [&](auto poly_tag) {
-        constexpr bool POLY = decltype(poly_tag)::value;
+      // exp, row sum, P store: P = 2^(bf16(s c - m c)) as bf16 pairs, summed in fp32 (the
+      // row sum adds the same values the PV MMA weights V with).
 #pragma unroll
-        for (int k = 0; k < BN; k += 16) {
-          uint32_t pk[8];
+      for (int k = 0; k < BN; k += 16) {
+        uint32_t pk[8];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const float2 y = f2fma(make_float2(x[k + 2 * t], x[k + 2 * t + 1]), cc, nmc);
-            const float2 e = (POLY && t >= 5) ? ex2_poly2(y) : make_float2(ex2(y.x), ex2(y.y));
-            sum2[t & 3] = f2add(sum2[t & 3], e);
-            pk[t] = pack_bf16x2(e.x, e.y);
-          }
-          tmem_st8(s_addr + k / 2, pk);        // P (bf16 pairs) over S's first 64 columns
-          if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
-          }
+        for (int t = 0; t < 8; ++t) {
+          const float2 y = f2fma(make_float2(x[k + 2 * t], x[k + 2 * t + 1]), cc, nmc);
+          const uint32_t eb = ex2_bf16x2(pack_bf16x2(y.x, y.y));
+          sum2[t & 3] = f2add(sum2[t & 3], make_float2(__uint_as_float(eb << 16),
+                                                       __uint_as_float(eb & 0xFFFF0000u)));
+          pk[t] = eb;
         }
-      };
-      if (masked) {
-        exp_store(std::false_type{});   // tiles with masked keys: every exp on MUFU
-      } else {
-        exp_store(std::true_type{});
+        tmem_st8(s_addr + k / 2, pk);        // P (bf16 pairs) over S's first 64 columns
+        if (k == BN / 2 - 16 || k == BN - 16) {  // a half of the keys is done: release it
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_full[2 * ti + (k == BN - 16 ? 1 : 0)]);
+        }
       }
       const float2 s01 = f2add(sum2[0], sum2[1]), s23 = f2add(sum2[2], sum2[3]);
       l += (s01.x + s23.x) + (s01.y + s23.y);
