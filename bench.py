@@ -255,11 +255,12 @@ def _ops_side(hbm_peak, tc_peak, peak_kind):
     c = torch.empty_like(a)
     for _ in range(3):
         cuda_ops.gemm(a, b, out=c)
-    ms = _time_device(lambda: cuda_ops.gemm(a, b, out=c), 20, stream)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = _time_device(lambda: cuda_ops.gemm(a, b, out=c), 20, stream)
     tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
     res["gemm_bf16_8192"] = {"tflops": round(tf, 1), "ms": round(ms, 4),
                              "frac": round(tf / tc_peak, 4), "peak": tc_peak,
-                             "peak_kind": peak_kind + " burst"}
+                             "peak_kind": peak_kind + " burst", "clocks": clk.summary()}
     del a, b, c
     if os.environ.get("ENIGMA_BENCH_SDPA", "1") == "1" and _sdpa_tc_available():
         B, H, S, D = 8, 32, 8192, 128
@@ -271,12 +272,14 @@ def _ops_side(hbm_peak, tc_peak, peak_kind):
             fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
             for _ in range(2):
                 fn()
-            ms = _time_device(fn, 5, stream)
+            with ClockSampler(torch.cuda.current_device()) as clk:
+                ms = _time_device(fn, 5, stream)
             fl = (2 if causal else 4) * B * H * S * S * D
             tf = fl / (ms * 1e-3) / 1e12
             res[f"sdpa_bf16_{'causal' if causal else 'noncausal'}_8x32x8192x128"] = {
                 "tflops": round(tf, 1), "ms": round(ms, 3), "frac": round(tf / tc_peak, 4),
-                "flops_convention": "causal 2*B*H*S^2*D, non-causal 4*B*H*S^2*D"}
+                "flops_convention": "causal 2*B*H*S^2*D, non-causal 4*B*H*S^2*D",
+                "clocks": clk.summary()}
     res["decode_layer_config5"] = _decode_side(hbm_peak)
     return res
 
