@@ -26,13 +26,15 @@ def _run(cfg, seed=0):
     return layer, out.float().cpu().numpy(), ref, k, v
 
 
-@pytest.mark.parametrize("batch,hidden,hq,hkv,inter,cache", [
-    (2, 128, 2, 1, 256, 10), (64, 896, 14, 2, 4864, 2048), (5, 512, 8, 2, 1024, 300),
-    (1, 1024, 16, 8, 3072, 32)])
-def test_decode_layer(cuda, batch, hidden, hq, hkv, inter, cache):
+@pytest.mark.parametrize("batch,hidden,hq,hkv,inter,cache,cap", [
+    (2, 128, 2, 1, 256, 10, 74), (64, 896, 14, 2, 4864, 2048, 2112), (5, 512, 8, 2, 1024, 300, 364),
+    (1, 1024, 16, 8, 3072, 32, 96),
+    (128, 256, 4, 2, 512, 200, 264),     # the largest batch: a full 128-row A box
+    (3, 256, 4, 1, 512, 299, 300)])      # the appended key in the cache's last slot
+def test_decode_layer(cuda, batch, hidden, hq, hkv, inter, cache, cap):
     from enigma.decode_layer import DecodeConfig
     cfg = DecodeConfig(batch=batch, hidden=hidden, heads_q=hq, heads_kv=hkv, intermediate=inter,
-                       cache_len=cache, cache_capacity=cache + 64)
+                       cache_len=cache, cache_capacity=cap)
     layer, got, ref, k_new, v_new = _run(cfg)
     assert orc.max_abs(got, ref) <= 2e-2, orc.max_abs(got, ref)
     assert orc.rel_fro(got, ref) <= 5e-3, orc.rel_fro(got, ref)
