@@ -113,6 +113,11 @@ __device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
   return y;
 }
 
+#ifndef SDPA_HEAD_GROUP
+#define SDPA_HEAD_GROUP 8
+#endif
+constexpr int kHeadGroup = SDPA_HEAD_GROUP;
+
 template <int D>
 __global__ void __launch_bounds__(THREADS, 1)
 sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -139,8 +144,15 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const int lane = threadIdx.x & 31;
 
   // Heavy (late, for causal) query tiles first.
-  const int pair = p.num_ctas_q - 1 - int(blockIdx.x);
-  const int bh = int(blockIdx.y);             // b * Hq + h
+  // CTA order: groups of kHeadGroup (batch, head) pairs; inside a group the heaviest query
+  // pairs (late, for causal) of all its heads first.  Concurrent CTAs then share a few
+  // heads' K / V in L2, and the last CTAs to start are light ones.
+  const int nq = p.num_ctas_q, nbh = int(gridDim.x) / nq;
+  const int grp = int(blockIdx.x) / (kHeadGroup * nq);
+  const int in_grp = int(blockIdx.x) - grp * kHeadGroup * nq;
+  const int gsz = min(kHeadGroup, nbh - grp * kHeadGroup);
+  const int pair = nq - 1 - in_grp / gsz;
+  const int bh = grp * kHeadGroup + in_grp % gsz;   // b * Hq + h
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int bhk = b * p.Hkv + h / (p.Hq / p.Hkv);
   const int q0 = pair * 2 * BM;               // first row of Q0; Q1 starts at q0 + BM
@@ -463,7 +475,7 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.status = enigma::device_status();
-  dim3 grid(unsigned(p.num_ctas_q), unsigned(B * Hq));
+  dim3 grid(unsigned(int64_t(p.num_ctas_q) * B * Hq));
   sdpa_fwd_tc_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
