@@ -16,6 +16,7 @@ int sm_count();
 uint32_t* device_status();
 
 // Operator launchers (asynchronous).  Arguments are validated by the C ABI layer.
+cudaStream_t aux_stream();
 cudaError_t rmsnorm_launch(int dtype, const void* x, const void* w, void* y, int64_t rows,
                            int64_t hidden, float eps, cudaStream_t s);
 // Same, with the SM count given (no per-device state is touched).

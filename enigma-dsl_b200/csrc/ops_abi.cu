@@ -2,6 +2,8 @@
 // event timing.  Validation happens here; kernels assume valid arguments.
 #include <cstdio>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 using enigma::set_error;
@@ -39,6 +41,74 @@ int32_t enigma_rmsnorm(int32_t dtype, const void* x, const void* w, void* y, int
   if (!(eps >= 0.0f)) return bad("rmsnorm: eps must be >= 0");
   return launch_status(
       enigma::rmsnorm_launch(dtype, x, w, y, rows, hidden, eps, as_stream(stream)), "rmsnorm");
+}
+
+// ---- RMSNorm of host-resident rows with overlapped transfers ----------------------------
+// Workspace: w, then two chunk sets (x chunk, y chunk), each 256-byte aligned.
+static size_t rms_host_ws(size_t es, int64_t hidden, int64_t chunk_rows) {
+  auto a256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+  return a256(size_t(hidden) * es) + 4 * a256(size_t(chunk_rows) * size_t(hidden) * es);
+}
+
+int32_t enigma_rmsnorm_host_workspace_bytes(int32_t dtype, int64_t hidden, int64_t chunk_rows,
+                                            size_t* bytes) {
+  if (dtype != ENIGMA_DTYPE_F32 && dtype != ENIGMA_DTYPE_BF16) return bad("rmsnorm dtype");
+  if (hidden <= 0 || chunk_rows <= 0) return bad("rmsnorm_host: hidden and chunk_rows must be > 0");
+  if (bytes == nullptr) return bad("rmsnorm_host: bytes is NULL");
+  *bytes = rms_host_ws(dtype == ENIGMA_DTYPE_F32 ? 4 : 2, hidden, chunk_rows);
+  return ENIGMA_OK;
+}
+
+int32_t enigma_rmsnorm_host(int32_t dtype, const void* x_host, const void* w_host, void* y_host,
+                            int64_t rows, int64_t hidden, float eps, void* workspace,
+                            size_t workspace_bytes, int64_t chunk_rows, void* stream) {
+  if (dtype != ENIGMA_DTYPE_F32 && dtype != ENIGMA_DTYPE_BF16) return bad("rmsnorm dtype");
+  if (rows < 0 || hidden <= 0 || chunk_rows <= 0)
+    return bad("rmsnorm_host needs rows >= 0, hidden > 0, chunk_rows > 0");
+  if (!(eps >= 0.0f)) return bad("rmsnorm: eps must be >= 0");
+  if (rows == 0) return ENIGMA_OK;
+  if (x_host == nullptr || w_host == nullptr || y_host == nullptr || workspace == nullptr)
+    return bad("rmsnorm_host: NULL buffer");
+  const size_t es = dtype == ENIGMA_DTYPE_F32 ? 4 : 2;
+  if (!aligned(workspace, 256) || workspace_bytes < rms_host_ws(es, hidden, chunk_rows))
+    return bad("rmsnorm_host: workspace must be 256-byte aligned and at least "
+               "enigma_rmsnorm_host_workspace_bytes() bytes");
+  auto a256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* w_dev = ws;
+  const size_t chunk_bytes = a256(size_t(chunk_rows) * size_t(hidden) * es);
+  uint8_t* set0 = ws + a256(size_t(hidden) * es);
+  cudaStream_t st[2] = {as_stream(stream), enigma::aux_stream()};
+  if (st[1] == nullptr) return bad("rmsnorm_host: could not create the second stream");
+  const uint8_t* xh = static_cast<const uint8_t*>(x_host);
+  uint8_t* yh = static_cast<uint8_t*>(y_host);
+  cudaEvent_t ready = nullptr, done = nullptr;
+  cudaError_t e = cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
+  // w once on the caller's stream; the second stream starts after it.
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(w_dev, w_host, size_t(hidden) * es, cudaMemcpyHostToDevice, st[0]);
+  if (e == cudaSuccess) e = cudaEventRecord(ready, st[0]);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st[1], ready, 0);
+  // Chunk c on stream c % 2 with buffer set c % 2: upload, kernel, download in stream order,
+  // so one stream's upload overlaps the other's kernel and download (PCIe is full duplex).
+  for (int64_t r0 = 0, c = 0; e == cudaSuccess && r0 < rows; r0 += chunk_rows, ++c) {
+    const int64_t n = std::min<int64_t>(chunk_rows, rows - r0);
+    const size_t off = size_t(r0) * size_t(hidden) * es, nb = size_t(n) * size_t(hidden) * es;
+    uint8_t* xd = set0 + (c & 1) * 2 * chunk_bytes;
+    uint8_t* yd = xd + chunk_bytes;
+    cudaStream_t sc = st[c & 1];
+    e = cudaMemcpyAsync(xd, xh + off, nb, cudaMemcpyHostToDevice, sc);
+    if (e == cudaSuccess) e = enigma::rmsnorm_launch(dtype, xd, w_dev, yd, n, hidden, eps, sc);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(yh + off, yd, nb, cudaMemcpyDeviceToHost, sc);
+  }
+  // The caller's stream ends after both; the call returns when everything is done.
+  if (e == cudaSuccess) e = cudaEventRecord(done, st[1]);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(st[0], done, 0);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st[0]);
+  if (ready) cudaEventDestroy(ready);
+  if (done) cudaEventDestroy(done);
+  return launch_status(e, "rmsnorm_host");
 }
 
 int32_t enigma_elementwise(int32_t op, int32_t dtype, const void* A, const void* B, void* C,

@@ -20,6 +20,7 @@ std::mutex g_mu;
 constexpr int kMaxDev = 64;
 int g_sms[kMaxDev] = {0};
 uint32_t* g_status[kMaxDev] = {nullptr};
+cudaStream_t g_aux[kMaxDev] = {nullptr};
 
 int current_device() {
   int d = 0;
@@ -63,6 +64,17 @@ uint32_t* device_status() {
   const int d = current_device();
   if (ensure_device_state(d) != cudaSuccess) return nullptr;
   return g_status[d];
+}
+
+// A library-owned non-blocking stream of the current device, for work a call overlaps with
+// the caller's stream (created on first use, never destroyed).
+cudaStream_t aux_stream() {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDev) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_aux[d] == nullptr && cudaStreamCreateWithFlags(&g_aux[d], cudaStreamNonBlocking) != cudaSuccess)
+    g_aux[d] = nullptr;
+  return g_aux[d];
 }
 
 }  // namespace enigma

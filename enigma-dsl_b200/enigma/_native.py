@@ -59,6 +59,8 @@ PROTOTYPES = {
                             _c.POINTER(_i64), _f32, _i32, _vp],
     "enigma_sdpa_strided_sinks": [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                   _i64, _c.POINTER(_i64), _f32, _i32, _vp, _vp],
+    "enigma_rmsnorm_host_workspace_bytes": [_i32, _i64, _i64, _c.POINTER(_sz)],
+    "enigma_rmsnorm_host": [_i32, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _sz, _i64, _vp],
     "enigma_decode_workspace_bytes": [_vp, _c.POINTER(_sz)],
     "enigma_decode_layer_bf16": [_vp, _vp, _vp, _vp, _sz, _vp],
     "enigma_qwen_decode_f32": [_vp, _vp],

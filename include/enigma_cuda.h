@@ -136,6 +136,21 @@ int32_t enigma_sdpa_strided_sinks(int32_t dtype, const void* Q, const void* K, c
                                   const int64_t* strides12, float scale, int32_t causal,
                                   const float* sinks, void* stream);
 
+/* ---- RMSNorm of host-resident rows (the reference's execute() path: host arrays in, host
+ *      bytes out, runtime.py:318-421, for the RMSNorm of examples/benchmark_rmsnorm.py) ----
+ * x_host [rows, hidden] -> y_host, w_host [hidden]; dtype ENIGMA_DTYPE_F32 or _BF16.  Rows go
+ * through the GPU in chunks of chunk_rows on two streams (the caller's and a library-owned
+ * one): chunk c's upload, kernel and download run in order on stream c % 2, so uploads,
+ * kernels and downloads of neighbouring chunks overlap (host<->device copies are full
+ * duplex).  x_host / y_host should be page-locked (enigma_host_alloc) for the copies to
+ * overlap.  workspace: device memory of enigma_rmsnorm_host_workspace_bytes() bytes, 256-byte
+ * aligned (w and two chunk buffers each way).  Synchronous: returns when y_host is written. */
+int32_t enigma_rmsnorm_host_workspace_bytes(int32_t dtype, int64_t hidden, int64_t chunk_rows,
+                                            size_t* bytes);
+int32_t enigma_rmsnorm_host(int32_t dtype, const void* x_host, const void* w_host, void* y_host,
+                            int64_t rows, int64_t hidden, float eps, void* workspace,
+                            size_t workspace_bytes, int64_t chunk_rows, void* stream);
+
 /* ---- one decoder-layer decode step (Qwen-style; the reference's qwen_fused megakernel,
  *      examples/qwen_megakernel.py:228-269, at BASELINE config 5 shapes) ----
  * x, out: [batch, hidden] bf16.  Weights bf16, row-major [in, out]:

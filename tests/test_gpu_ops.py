@@ -147,3 +147,44 @@ def test_sdpa_f32_fa_d4(cuda):
     o = cuda_ops.sdpa(_t(q, torch.float32, cuda), _t(k, torch.float32, cuda),
                       _t(v, torch.float32, cuda), scale=0.5)
     np.testing.assert_allclose(_np(o), orc.sdpa(q, k, v, 0.5), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("rows,hidden,chunk,pinned,dtype", [
+    (1000, 512, 300, True, "bf16"), (1000, 512, 300, False, "bf16"), (7, 4096, 2, True, "f32"),
+    (4096, 4096, 4096, True, "f32"), (65536, 2048, 16384, True, "bf16")])
+def test_rmsnorm_host(cuda, rows, hidden, chunk, pinned, dtype):
+    """enigma_rmsnorm_host: host x / w in, host y out, chunked with overlapped copies."""
+    import ctypes
+    import torch
+    from enigma import _native
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((rows, hidden), dtype=np.float32)
+    w = (1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    if dtype == "bf16":
+        x, w = orc.bf16_round(x), orc.bf16_round(w)
+        tdt, code = torch.bfloat16, _native.DTYPE_BF16
+    else:
+        tdt, code = torch.float32, _native.DTYPE_F32
+    hx = torch.from_numpy(x).to(tdt)
+    hw = torch.from_numpy(w).to(tdt)
+    hy = torch.empty_like(hx)
+    if pinned:
+        hx, hw, hy = hx.pin_memory(), hw.pin_memory(), hy.pin_memory()
+    lib = _native.lib()
+    wsb = ctypes.c_size_t()
+    _native.check(lib.enigma_rmsnorm_host_workspace_bytes(code, hidden, chunk, ctypes.byref(wsb)),
+                  "ws")
+    ws = torch.empty(wsb.value, dtype=torch.uint8, device=cuda)
+    _native.check(lib.enigma_rmsnorm_host(code, hx.data_ptr(), hw.data_ptr(), hy.data_ptr(), rows,
+                                          hidden, 1e-6, ws.data_ptr(), wsb.value, chunk, None),
+                  "rmsnorm_host")
+    ref = orc.rmsnorm(x, w, 1e-6)
+    got = hy.float().numpy()
+    if dtype == "bf16":
+        assert np.all(np.abs(got - ref) <= np.abs(ref) * 2.0 ** -8 + 1e-6)
+    else:
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+    with pytest.raises(_native.EnigmaCudaError, match="workspace"):
+        _native.check(lib.enigma_rmsnorm_host(code, hx.data_ptr(), hw.data_ptr(), hy.data_ptr(),
+                                              rows, hidden, 1e-6, ws.data_ptr(), 16, chunk, None),
+                      "rmsnorm_host")
