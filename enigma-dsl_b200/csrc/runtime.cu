@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace enigma {
 
@@ -78,6 +79,21 @@ cudaStream_t aux_stream() {
 }
 
 }  // namespace enigma
+
+namespace {
+// Self-test of the failure reporting: one thread waits on an mbarrier that nothing arrives
+// on, gives up after `polls` polls exactly as the kernels' bounded waits do (flag the device
+// status word, return), so the host side of a timeout can be exercised without hanging.
+__global__ void timeout_probe_kernel(uint32_t* status, long long polls) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  enigma_sm100::mbar_init(&bar, 1);
+  enigma_sm100::fence_barrier_init();
+  for (long long i = 0; i < polls; ++i)
+    if (enigma_sm100::mbar_try_wait(&bar, 0)) return;   // never completes: nothing arrives
+  atomicExch(status, enigma_sm100::kDevTimeout);
+}
+}  // namespace
 
 using enigma::set_error;
 
@@ -189,6 +205,14 @@ int32_t enigma_take_device_status(int32_t* timeouts) {
   if (v != 0) cudaMemset(st, 0, sizeof(uint32_t));
   if (timeouts) *timeouts = static_cast<int32_t>(v);
   return ENIGMA_OK;
+}
+
+int32_t enigma_check_timeout_path(int64_t polls, void* stream) {
+  if (polls < 0 || polls > (int64_t(1) << 24)) return badarg("polls must be in [0, 2^24]");
+  uint32_t* st = enigma::device_status();
+  if (st == nullptr) return cuda_status(cudaErrorNoDevice, "device status");
+  timeout_probe_kernel<<<1, 32, 0, as_stream(stream)>>>(st, static_cast<long long>(polls));
+  return cuda_status(cudaGetLastError(), "timeout probe");
 }
 
 int32_t enigma_synchronize(void* stream) {

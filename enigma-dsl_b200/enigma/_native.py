@@ -75,6 +75,7 @@ PROTOTYPES = {
     "enigma_event_record": [_vp, _vp],
     "enigma_event_elapsed_ms": [_vp, _vp, _c.POINTER(_f32)],
     "enigma_take_device_status": [_c.POINTER(_i32)],
+    "enigma_check_timeout_path": [_i64, _vp],
 }
 
 

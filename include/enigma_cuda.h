@@ -225,6 +225,11 @@ int32_t enigma_event_elapsed_ms(void* start, void* stop, float* ms);
 
 /* Number of device-side timeouts flagged since the last call (and reset). */
 int32_t enigma_take_device_status(int32_t* timeouts);
+/* Self-test of the timeout reporting: enqueues one CTA that waits on a barrier nothing
+ * arrives on, gives up after `polls` polls (<= 2^24; microseconds) and flags the device status
+ * word as the kernels' bounded waits do; the next enigma_synchronize then returns
+ * ENIGMA_ERR_TIMEOUT and clears it, and the context stays usable. */
+int32_t enigma_check_timeout_path(int64_t polls, void* stream);
 
 #ifdef __cplusplus
 }
