@@ -426,7 +426,7 @@ def run_ours(args):
     # uploads, kernels and downloads overlap on two streams.
     lib = _native.lib()
     nbytes = ROWS * HIDDEN * 2
-    chunk = 16384
+    chunk = 8192
     hx = torch.empty((ROWS, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
     hy = torch.empty((ROWS, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
     hw = torch.empty((HIDDEN,), dtype=torch.bfloat16, pin_memory=True)
@@ -471,7 +471,7 @@ def run_ours(args):
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s (algorithmic bytes / e2e time)",
                 "h2d_bytes_per_step": nbytes + HIDDEN * 2, "d2h_bytes_per_step": nbytes,
                 "ms_per_step": round(e2e_ms, 3),
-                "path": "C ABI enigma_rmsnorm_host: pinned host in / out, 16384-row chunks, "
+                "path": "C ABI enigma_rmsnorm_host: pinned host in / out, 8192-row chunks, "
                         "uploads / kernels / downloads overlapped on two streams"},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
