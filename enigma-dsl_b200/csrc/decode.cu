@@ -6,18 +6,19 @@
 // + residual).  At batch 64 every GEMM is skinny (M = 64) and the step is bound
 // by HBM: ~30 MB of weights and ~67 MB of KV cache per step.  So:
 //
-//   * GEMMs are split-K tcgen05 kernels: grid (N/64 tiles, K splits) fills the
-//     148 SMs even for N = 896; each CTA streams its K range of B through a TMA
-//     ring and writes an fp32 128x64 partial tile to a workspace.
-//   * The split reduction is fused with what follows each GEMM: RoPE + KV-cache
-//     append (QKV), residual add + RMSNorm (O-proj), SwiGLU (gate/up), residual
-//     add (down-proj).
+//   * Each GEMM is one cluster launch: grid (N/64 tiles, cs) with cluster (1, cs), the
+//     cs CTAs of a cluster split the tile's k-blocks, accumulate in TMEM and sum their
+//     partial tiles over distributed shared memory, so the whole grid fills the 148 SMs
+//     even for N = 896 and no partial goes through global memory.
+//   * What follows each GEMM runs in its epilogue: RoPE + KV-cache append (QKV),
+//     residual add + the post-attention RMSNorm's weight and row sums of squares
+//     (O-proj), the RMSNorm factor + SwiGLU (gate/up), residual add (down-proj).
 //   * Attention is split-KV ("flash decoding") in one persistent kernel: CTAs stream
 //     balanced ranges of (sequence x kv head, 128-key chunk) pairs through a TMA ring,
 //     and the CTA that finishes a (sequence, kv head) merges its partials.
 //
-// Workspace (caller-owned, enigma_decode_workspace_bytes) holds every partial
-// and intermediate, so a step makes no allocation.
+// Workspace (caller-owned, enigma_decode_workspace_bytes) holds every intermediate and the
+// attention partials, so a step makes no allocation.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -33,108 +34,307 @@ namespace {
 using namespace enigma_sm100;
 using namespace enigma_decode;
 
-constexpr int SK_THREADS = 192;
-constexpr int SK_SMEM = SK_RING + 1024;
-
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// One split-K item per CTA: blockIdx = (N tile, split).
-__global__ void __launch_bounds__(SK_THREADS)
-gemm_splitk_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      float* __restrict__ partial, int M, int N, int K, int kb_per_split,
-                      int a_rows, uint32_t* status) {
+// ============================================================================ cluster split-K
+// One GEMM of the step with its epilogue in a single launch.  Grid (tiles, cs) with cluster
+// dims (1, cs, 1): the cs CTAs of a cluster share one output tile (64 columns, or 64 gate +
+// 64 up columns) and split its k-blocks evenly.  Each CTA accumulates its K range in TMEM,
+// drains it into its own shared memory (the drained ring), and after a cluster barrier CTA r
+// sums rows [r R, (r + 1) R) of all cs partials over distributed shared memory, in rank
+// order (deterministic), and applies the epilogue to them.  No partials go through global
+// memory and no separate reduction kernel runs.
+enum : int { EPI_QKV = 0, EPI_OPROJ = 1, EPI_GATEUP = 2, EPI_DOWN = 3 };
+
+struct EpiArgs {
+  int M;                                // rows (batch)
+  // EPI_QKV: RoPE on q / k heads, q to q_out, k / v appended at `pos`, counters zeroed
+  int Hq, Hkv, s_cap, pos;
+  const float* cosv;
+  const float* sinv;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* kc;
+  __nv_bfloat16* vc;
+  uint32_t* counters;
+  // EPI_OPROJ: h = acc + residual -> h_out; h * w_norm -> hw_out; row sums of h^2 of this
+  // tile -> ssq[tile][m].  EPI_DOWN: acc + residual -> h_out.
+  int ld;                               // row pitch of residual / h_out / hw_out (hidden)
+  const __nv_bfloat16* residual;
+  __nv_bfloat16* h_out;
+  const __nv_bfloat16* w_norm;
+  __nv_bfloat16* hw_out;
+  float* ssq;                           // [tiles][128]
+  // EPI_GATEUP: r = 1 / sqrt(sum_t ssq[t][m] / ld + eps) (s_rs); act = silu(r g) * (r u)
+  int I, ssq_tiles;
+  float eps;
+  __nv_bfloat16* act;
+};
+
+constexpr int CK_THREADS = 192;
+constexpr int CK_MAX_CLUSTER = 8;    // portable cluster size
+
+template <int NB>
+struct CkShape {
+  static constexpr int STAGES = NB == 1 ? 4 : 3;
+  static constexpr int B_BYTES = NB * SK_BK * 64 * 2;              // 8 KB per 64 columns
+  static constexpr int STAGE = SK_A_BYTES + B_BYTES;
+  static constexpr int RING = STAGES * STAGE;                        // 96 KB
+  static constexpr int PSTRIDE = NB * 64 + 4;                        // floats per partial row
+  static constexpr int SMEM = RING + 1024;
+  static_assert(SK_BM * PSTRIDE * 4 <= RING, "partial tile must fit in the drained ring");
+};
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float4 bf16x4_f4(const __nv_bfloat16* p) {
+  const uint2 r = *reinterpret_cast<const uint2*>(p);
+  return make_float4(bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y));
+}
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float a, float b, float c, float d) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+}
+
+// The epilogue of one item: row m, four columns 4 g.. of the tile (a0), and the matching
+// four of the second 64 columns (gate|up: the up half) or, for QKV, columns 4 g + 32.. (a1).
+// All threads call it (shuffles); `valid` marks a real item.
+template <int EPI>
+__device__ __forceinline__ void ck_epilogue(const EpiArgs& e, int tile, int m, int g, bool valid,
+                                            float4 a0, float4 a1, const float* s_rs) {
+  if constexpr (EPI == EPI_QKV) {
+    constexpr int D = 64, H2 = 32;
+    if (!valid || g >= 8) return;
+    const int head = tile, d = 4 * g;
+    if (head >= e.Hq && head < e.Hq + e.Hkv && g == 0) e.counters[m * e.Hkv + head - e.Hq] = 0u;
+    float lo[4] = {a0.x, a0.y, a0.z, a0.w}, hi[4] = {a1.x, a1.y, a1.z, a1.w};
+    if (head < e.Hq + e.Hkv) {   // RoPE, rotate-half pairing d <-> d + 32
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float l2 = lo[t] * e.cosv[d + t] - hi[t] * e.sinv[d + t];
+        const float h2 = hi[t] * e.cosv[d + t + H2] + lo[t] * e.sinv[d + t + H2];
+        lo[t] = l2;
+        hi[t] = h2;
+      }
+    }
+    __nv_bfloat16* dst;
+    if (head < e.Hq) {
+      dst = e.q_out + (int64_t(m) * e.Hq + head) * D;
+    } else {
+      const int kvh = head < e.Hq + e.Hkv ? head - e.Hq : head - e.Hq - e.Hkv;
+      __nv_bfloat16* cache = head < e.Hq + e.Hkv ? e.kc : e.vc;
+      dst = cache + ((int64_t(m) * e.Hkv + kvh) * e.s_cap + e.pos) * D;
+    }
+    st_bf16x4(dst + d, lo[0], lo[1], lo[2], lo[3]);
+    st_bf16x4(dst + d + H2, hi[0], hi[1], hi[2], hi[3]);
+  } else if constexpr (EPI == EPI_OPROJ) {
+    const int col = tile * 64 + 4 * g;
+    float ss = 0.f;
+    if (valid) {
+      const int64_t o = int64_t(m) * e.ld + col;
+      const float4 r = bf16x4_f4(e.residual + o);
+      const float4 h = f4add(a0, r);
+      st_bf16x4(e.h_out + o, h.x, h.y, h.z, h.w);
+      const float4 w = bf16x4_f4(e.w_norm + col);
+      st_bf16x4(e.hw_out + o, h.x * w.x, h.y * w.y, h.z * w.z, h.w * w.w);
+      ss = h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (valid && g == 0) e.ssq[tile * 128 + m] = ss;
+  } else if constexpr (EPI == EPI_GATEUP) {
+    const int j = tile * 64 + 4 * g;
+    if (!valid || j >= e.I) return;
+    const float r = s_rs[m];
+    auto sw = [r](float gg, float uu) {
+      gg *= r;
+      return gg / (1.0f + __expf(-gg)) * (uu * r);
+    };
+    st_bf16x4(e.act + int64_t(m) * e.I + j, sw(a0.x, a1.x), sw(a0.y, a1.y), sw(a0.z, a1.z),
+              sw(a0.w, a1.w));
+  } else {
+    if (!valid) return;
+    const int64_t o = int64_t(m) * e.ld + tile * 64 + 4 * g;
+    const float4 h = f4add(a0, bf16x4_f4(e.residual + o));
+    st_bf16x4(e.h_out + o, h.x, h.y, h.z, h.w);
+  }
+}
+
+// Warp roles: warp 0 producer (one thread), warp 1 TMEM owner + MMA issuer (one thread),
+// warps 2..5 drain TMEM lanes 32 (warp % 4).. into the partial tile; then all six warps reduce.
+template <int EPI, int NB>
+__global__ void __launch_bounds__(CK_THREADS)
+gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const EpiArgs ea, int num_kb, int a_rows, int b_col2, uint32_t* status) {
+  using S = CkShape<NB>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bars[2 * SK_STAGES + 2];
+  __shared__ uint64_t full[S::STAGES], empty[S::STAGES], acc_full;
   __shared__ uint32_t tmem_slot;
-  const SkRing r{align1024(smem_raw), bars, bars + SK_STAGES, bars + 2 * SK_STAGES,
-                 bars + 2 * SK_STAGES + 1};
+  __shared__ float s_rs[SK_BM];           // EPI_GATEUP: RMSNorm factor of each row
+  uint8_t* ring = align1024(smem_raw);
+  auto a_slot = [&](int s) { return ring + s * S::STAGE; };
+  auto b_slot = [&](int s) { return ring + s * S::STAGE + SK_A_BYTES; };
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const SkItem w = sk_item(blockIdx.y * gridDim.x + blockIdx.x, gridDim.x, kb_per_split,
-                           (K + SK_BK - 1) / SK_BK);
+  const int tile = blockIdx.x;
+  const int cs = int(gridDim.y), rank = int(cluster_ctarank());
+  const int kb0 = rank * num_kb / cs, kb1 = (rank + 1) * num_kb / cs, nkb = kb1 - kb0;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    sk_ring_init(r);
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_slot, SK_BN);
+    tmem_alloc(&tmem_slot, NB * 64);
     tmem_relinquish();
   }
-  sk_zero_pad(r, a_rows, threadIdx.x, SK_THREADS);
+  if (a_rows < SK_BM) {   // rows a_rows..127 of every A slot stay zero (TMA never writes them)
+    const int per = (SK_BM - a_rows) * 8;
+    for (int i = threadIdx.x; i < S::STAGES * per; i += CK_THREADS)
+      reinterpret_cast<uint4*>(a_slot(i / per) + a_rows * 128)[i % per] = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  // The first stages' weight tiles go to shared memory and the rest of this CTA's slice to
-  // L2 before waiting on the predecessor, so the weight stream overlaps its tail.
-  int pre = 0;
+  const uint32_t tx = uint32_t(a_rows * SK_BK * 2 + S::B_BYTES);
+  auto load_b = [&](int s, int kb) {
+    tma_load_2d(b_slot(s), &tmB, &full[s], tile * 64, kb * SK_BK);
+    if constexpr (NB == 2) tma_load_2d(b_slot(s) + 8192, &tmB, &full[s], b_col2 + tile * 64, kb * SK_BK);
+  };
+  // Weights never depend on the previous kernel: the first stages' tiles and an L2 prefetch
+  // of the rest of the slice are issued before waiting on it.
+  const int pre = nkb < S::STAGES ? nkb : S::STAGES;
   if (warp == 0 && lane == 0) {
-    pre = sk_produce_pre(r, &tmB, w, a_rows, 0, status);
-    for (int kb = w.kb0 + pre; kb < w.kb1; ++kb) tma_prefetch_l2_2d(&tmB, w.nb * SK_BN, kb * SK_BK);
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], tx);
+      load_b(i, kb0 + i);
+    }
+    for (int kb = kb0 + pre; kb < kb1; ++kb) {
+      tma_prefetch_l2_2d(&tmB, tile * 64, kb * SK_BK);
+      if constexpr (NB == 2) tma_prefetch_l2_2d(&tmB, b_col2 + tile * 64, kb * SK_BK);
+    }
   }
-  griddep_wait();  // A (the previous kernel's output) and the partial buffer are ready / free
+  griddep_wait();   // A (the previous kernel's output) is ready
   if (warp == 0) {
     if (lane == 0) {
-      uint32_t it = 0;
-      sk_produce_rest(r, &tmA, &tmB, w, a_rows, pre, it, status);
+      for (int i = 0; i < pre; ++i) tma_load_2d(a_slot(i), &tmA, &full[i], (kb0 + i) * SK_BK, 0);
+      for (int i = pre; i < nkb; ++i) {
+        const int s = i % S::STAGES;
+        if (!mbar_wait(&empty[s], ((i / S::STAGES) & 1) ^ 1, status)) break;
+        mbar_arrive_expect_tx(&full[s], tx);
+        tma_load_2d(a_slot(s), &tmA, &full[s], (kb0 + i) * SK_BK, 0);
+        load_b(s, kb0 + i);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      uint32_t it = 0, acc = 0;
-      sk_mma(r, tmem, w, it, acc, status);
+    if (lane == 0 && nkb > 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(SK_BM, NB * 64, false, true);
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S::STAGES;
+        if (!mbar_wait(&full[s], (i / S::STAGES) & 1, status)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t da = smem_desc_sw128(smem_u32(a_slot(s)), 16, 1024);
+        const uint64_t db = smem_desc_sw128(smem_u32(b_slot(s)), 8192, 1024);
+#pragma unroll
+        for (int kk = 0; kk < SK_BK / 16; ++kk)
+          mma_bf16_ss(tmem, da + uint64_t((kk * 32) >> 4), db + uint64_t((kk * 2048) >> 4),
+                      idesc, (i | kk) ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      if (ok) mma_commit(&acc_full);
     }
     __syncwarp();
   } else {
-    uint32_t acc = 0;
-    sk_store(r, tmem, w, partial, M, N, warp & 3, lane, acc, status);
+    // Drain: TMEM lane = row; the ring is idle once the accumulator is complete.
+    const int q = warp & 3, row = q * 32 + lane;
+    if constexpr (EPI == EPI_GATEUP) {   // while the MMAs run
+      float t4[4] = {0.f, 0.f, 0.f, 0.f};
+      if (row < ea.M) {
+#pragma unroll 4
+        for (int t = 0; t < ea.ssq_tiles; ++t) t4[t & 3] += ea.ssq[t * 128 + row];
+      }
+      s_rs[row] = 1.0f / sqrtf(((t4[0] + t4[1]) + (t4[2] + t4[3])) / float(ea.ld) + ea.eps);
+    }
+    const bool ok = nkb == 0 || mbar_wait(&acc_full, 0, status);
+    tc_fence_after();
+    float* prow = reinterpret_cast<float*>(ring) + row * S::PSTRIDE;
+    const uint32_t taddr = tmem + (uint32_t(q * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < NB * 64; c += 16) {
+      uint32_t v[16];
+      if (nkb > 0 && ok) {
+        tmem_ld16(taddr + c, v);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = 0u;
+      }
+      if (row < ea.M) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          reinterpret_cast<float4*>(prow + c)[t] =
+              make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
+                          __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, SK_BN);
+    tmem_dealloc(tmem, NB * 64);
   }
-}
-
-// Grid (M, Hq + 2 Hkv), 32 threads: one (row, head) per CTA.
-__global__ void __launch_bounds__(32)
-qkv_finalize_kernel(const float* __restrict__ part, int splits, int M, int N, int Hq, int Hkv,
-                    const float* __restrict__ cosv, const float* __restrict__ sinv,
-                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kc,
-                    __nv_bfloat16* __restrict__ vc, int s_cap, int pos,
-                    uint32_t* __restrict__ attn_counters) {
-  griddep_launch_dependents();
-  griddep_wait();
-  qkv_finalize_item(part, splits, M, N, Hq, Hkv, cosv, sinv, q_out, kc, vc, s_cap, pos,
-                    attn_counters, blockIdx.x, blockIdx.y, threadIdx.x);
-}
-
-// One row per CTA of 256 threads.
-__global__ void __launch_bounds__(256)
-reduce_residual_norm_kernel(const float* __restrict__ part, int splits, int M, int N,
-                            const __nv_bfloat16* __restrict__ residual,
-                            __nv_bfloat16* __restrict__ h_out, const __nv_bfloat16* __restrict__ w,
-                            __nv_bfloat16* __restrict__ y_out, float eps) {
-  griddep_launch_dependents();
-  griddep_wait();
-  __shared__ float red[8];
-  reduce_residual_norm_row(part, splits, M, N, residual, h_out, w, y_out, eps, blockIdx.x,
-                           threadIdx.x, red);
-}
-
-// One float4 group (four columns) per thread.
-__global__ void __launch_bounds__(256)
-swiglu_kernel(const float* __restrict__ part, int splits, int M, int I,
-              __nv_bfloat16* __restrict__ act) {
-  griddep_launch_dependents();
-  griddep_wait();
-  const int64_t q = int64_t(blockIdx.x) * 256 + threadIdx.x;
-  if (q * 4 < int64_t(M) * I) swiglu_group(part, splits, M, I, act, q);
+  cluster_sync();   // every CTA's partial tile is complete and visible to the cluster
+  const int rows_per = (ea.M + cs - 1) / cs;
+  const int r0 = rank * rows_per;
+  const int r1 = min(ea.M, r0 + rows_per);
+  const uint32_t pbase = smem_u32(ring);
+  const int iters = (rows_per * 16 + CK_THREADS - 1) / CK_THREADS;
+  for (int itn = 0; itn < iters; ++itn) {
+    const int idx = itn * CK_THREADS + int(threadIdx.x);
+    const int m = r0 + idx / 16, g = idx % 16;
+    const bool valid = idx < rows_per * 16 && m < r1;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    if (valid) {
+      // All remote loads first, then the sums: each load is a cluster round trip.
+      const uint32_t off = pbase + uint32_t((m * S::PSTRIDE + 4 * g) * 4);
+      const uint32_t off2 = off + uint32_t((NB == 2 ? 64 : 32) * 4);
+      const bool second = NB == 2 || (EPI == EPI_QKV && g < 8);
+      float4 v0[CK_MAX_CLUSTER], v1[CK_MAX_CLUSTER];
+#pragma unroll
+      for (int p = 0; p < CK_MAX_CLUSTER; ++p) {
+        if (p < cs) {
+          v0[p] = ld_dsmem_f4(mapa_shared(off, uint32_t(p)));
+          if (second) v1[p] = ld_dsmem_f4(mapa_shared(off2, uint32_t(p)));
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < CK_MAX_CLUSTER; ++p) {
+        if (p < cs) {
+          a0 = f4add(a0, v0[p]);
+          if (second) a1 = f4add(a1, v1[p]);
+        }
+      }
+    }
+    ck_epilogue<EPI>(ea, tile, m, g, valid, a0, a1, s_rs);
+  }
+  cluster_sync();   // peers have finished reading this CTA's partial tile
 }
 
 // Persistent split-KV attention: one producer + DA_WARPS consumer warps per CTA, CTA c of
@@ -205,27 +405,23 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Split-K factor: about one (tile, split) CTA per SM, at least 2 k-blocks per split.
-int pick_splits(int64_t N, int64_t K, int sms) {
-  const int64_t tiles = (N + SK_BN - 1) / SK_BN;
-  const int64_t kbs = (K + SK_BK - 1) / SK_BK;
-  int64_t s = (int64_t(sms) + tiles - 1) / tiles;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, kbs / 2));
-  return int(std::max<int64_t>(1, s));
+// Cluster size of a GEMM: double it (up to CK_MAX_CLUSTER, and at most one k-block per CTA) while the
+// tiles x cluster CTAs do not yet cover the SMs.
+int pick_cluster(int64_t tiles, int64_t kbs, int sms) {
+  int cs = 1;
+  while (cs * 2 <= CK_MAX_CLUSTER && cs * 2 <= kbs && tiles * cs < sms) cs *= 2;
+  return cs;
 }
 
 struct Layout {
-  size_t partial, xn, q, attn, h1, h1n, act, opart, mlpart, counters, total;
+  size_t xn, q, attn, h1, h1w, act, ssq, opart, mlpart, counters, total;
   int attn_splits;
 };
 
-Layout plan(const enigma_decode_layer_desc& d, int sms) {
+Layout plan(const enigma_decode_layer_desc& d) {
   const int64_t B = d.batch, H = d.hidden, D = d.head_dim, Hq = d.heads_q, Hkv = d.heads_kv;
-  const int64_t I = d.intermediate, Nqkv = (Hq + 2 * Hkv) * D;
+  const int64_t I = d.intermediate;
   const int64_t L = d.position + 1;
-  const int64_t gemms[4][2] = {{Nqkv, H}, {H, Hq * D}, {2 * I, H}, {H, I}};
-  int64_t part = 0;
-  for (auto& g : gemms) part = std::max(part, pick_splits(g[0], g[1], sms) * B * g[0]);
   Layout l;
   // Attention CTAs take 128-key chunks of one (sequence, kv head); the partial buffers
   // are sized for the cache capacity, so one workspace serves every position.
@@ -234,13 +430,13 @@ Layout plan(const enigma_decode_layer_desc& d, int sms) {
   const int64_t G = Hq / Hkv;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align256(off + bytes); return o; };
-  l.partial = take(size_t(part) * 4);
   l.xn = take(size_t(B * H) * 2);
   l.q = take(size_t(B * Hq * D) * 2);
   l.attn = take(size_t(B * Hq * D) * 2);
   l.h1 = take(size_t(B * H) * 2);
-  l.h1n = take(size_t(B * H) * 2);
+  l.h1w = take(size_t(B * H) * 2);
   l.act = take(size_t(B * I) * 2);
+  l.ssq = take(size_t(H / 64) * 128 * 4);
   l.opart = take(size_t(B * Hkv * smax * G * D) * 4);
   l.mlpart = take(size_t(B * Hkv * smax * G * 2) * 4);
   l.counters = take(size_t(B * Hkv) * 4);
@@ -248,21 +444,38 @@ Layout plan(const enigma_decode_layer_desc& d, int sms) {
   return l;
 }
 
-cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M, int64_t N,
-                        int64_t K, int splits, uint32_t* status, cudaStream_t s) {
+// C-tile columns [tile * 64, +64) of A [M, K] x Bw [K, n_cols] (and, NB = 2, columns
+// b_col2 + tile * 64 ..) with epilogue EPI, as one cluster launch.
+template <int EPI, int NB>
+cudaError_t cluster_gemm(const void* A, const void* Bw, int64_t M, int64_t n_cols, int64_t K,
+                         int64_t tiles, int b_col2, const EpiArgs& ea, int sms, uint32_t* status,
+                         cudaStream_t s) {
+  using S = CkShape<NB>;
   CUtensorMap ta, tb;
   const int a_rows = int(std::min<int64_t>(SK_BM, (M + 7) / 8 * 8));
   if (!make_tmap_bf16_2d(&ta, A, M, K, K, SK_BK, uint32_t(a_rows)) ||
-      !make_tmap_bf16_2d(&tb, Bw, K, N, N, SK_BN, SK_BK))
+      !make_tmap_bf16_2d(&tb, Bw, K, n_cols, n_cols, 64, SK_BK))
     return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(gemm_splitk_tc_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM);
+  auto kern = gemm_cluster_kernel<EPI, NB>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
   if (e != cudaSuccess) return e;
-  const int kbs = int((K + SK_BK - 1) / SK_BK);
-  const int per = (kbs + splits - 1) / splits;
-  dim3 grid(unsigned((N + SK_BN - 1) / SK_BN), unsigned(splits));
-  return launch_pdl(gemm_splitk_tc_kernel, grid, dim3(SK_THREADS), SK_SMEM, s, ta, tb, partial,
-                    int(M), int(N), int(K), per, a_rows, status);
+  const int64_t kbs = (K + SK_BK - 1) / SK_BK;
+  const int cs = pick_cluster(tiles, kbs, sms);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(tiles), unsigned(cs));
+  cfg.blockDim = dim3(CK_THREADS);
+  cfg.dynamicSmemBytes = S::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = unsigned(cs);
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, ea, int(kbs), a_rows, b_col2, status);
 }
 
 }  // namespace
@@ -270,31 +483,36 @@ cudaError_t splitk_gemm(const void* A, const void* Bw, float* partial, int64_t M
 // The whole step with an explicit SM count and status word (no per-device state used).
 cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, void* out,
                              void* ws, int sms, uint32_t* status, cudaStream_t s) {
-  const Layout l = plan(d, sms);
+  const Layout l = plan(d);
   uint8_t* w = static_cast<uint8_t*>(ws);
-  float* part = reinterpret_cast<float*>(w + l.partial);
   auto bfp = [&](size_t o) { return reinterpret_cast<__nv_bfloat16*>(w + o); };
   const int B = int(d.batch), H = int(d.hidden), D = int(d.head_dim);
   const int Hq = int(d.heads_q), Hkv = int(d.heads_kv), I = int(d.intermediate);
   const int Nqkv = (Hq + 2 * Hkv) * D;
-  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
   cudaError_t e;
 #define ENIGMA_TRY(expr)           \
   do {                             \
     e = (expr);                    \
     if (e != cudaSuccess) return e; \
   } while (0)
+  EpiArgs ea = {};
+  ea.M = B;
   // 1. input RMSNorm
   ENIGMA_TRY(rmsnorm_launch_sms(ENIGMA_DTYPE_BF16, x, d.w_in_norm, bfp(l.xn), B, H, d.eps, sms, s));
-  // 2-3. QKV projection, RoPE, KV-cache append at `position`
-  int sp = pick_splits(Nqkv, H, sms);
-  ENIGMA_TRY(splitk_gemm(bfp(l.xn), d.w_qkv, part, B, Nqkv, H, sp, status, s));
-  ENIGMA_TRY(launch_pdl(qkv_finalize_kernel, dim3(B, Hq + 2 * Hkv), dim3(32), 0, s,
-                        static_cast<const float*>(part), sp, B, Nqkv, Hq, Hkv, d.rope_cos,
-                        d.rope_sin, bfp(l.q), static_cast<__nv_bfloat16*>(d.k_cache),
-                        static_cast<__nv_bfloat16*>(d.v_cache), int(d.cache_capacity),
-                        int(d.position), reinterpret_cast<uint32_t*>(w + l.counters)));
-  // 4. attention over position + 1 keys (split-KV, combined by each unit's last CTA)
+  // 2. QKV projection + RoPE + KV-cache append at `position` (+ attention counters zeroed)
+  ea.Hq = Hq;
+  ea.Hkv = Hkv;
+  ea.s_cap = int(d.cache_capacity);
+  ea.pos = int(d.position);
+  ea.cosv = d.rope_cos;
+  ea.sinv = d.rope_sin;
+  ea.q_out = bfp(l.q);
+  ea.kc = static_cast<__nv_bfloat16*>(d.k_cache);
+  ea.vc = static_cast<__nv_bfloat16*>(d.v_cache);
+  ea.counters = reinterpret_cast<uint32_t*>(w + l.counters);
+  ENIGMA_TRY((cluster_gemm<EPI_QKV, 1>(bfp(l.xn), d.w_qkv, B, Nqkv, H, Nqkv / 64, 0, ea, sms,
+                                      status, s)));
+  // 3. attention over position + 1 keys (split-KV, combined by each unit's last CTA)
   {
     CUtensorMap tk, tv;
     const uint64_t rows = uint64_t(B) * Hkv * uint64_t(d.cache_capacity);
@@ -313,32 +531,34 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
                           int(d.cache_capacity), int(d.position + 1), l.attn_splits, B * Hkv,
                           d.attn_scale * 1.4426950408889634f, status));
   }
-  // 6-7. O projection + residual(x) -> h1, post-attention RMSNorm -> h1n
-  sp = pick_splits(H, Hq * D, sms);
-  ENIGMA_TRY(splitk_gemm(bfp(l.attn), d.w_o, part, B, H, Hq * D, sp, status, s));
-  ENIGMA_TRY(launch_pdl(reduce_residual_norm_kernel, dim3(B), dim3(256), 0, s,
-                        static_cast<const float*>(part), sp, B, H, xb, bfp(l.h1),
-                        static_cast<const __nv_bfloat16*>(d.w_post_norm), bfp(l.h1n), d.eps));
-  // 8-9. gate|up projection, SwiGLU
-  sp = pick_splits(2 * I, H, sms);
-  ENIGMA_TRY(splitk_gemm(bfp(l.h1n), d.w_gate_up, part, B, 2 * I, H, sp, status, s));
-  ENIGMA_TRY(launch_pdl(swiglu_kernel, dim3(unsigned((int64_t(B) * I / 4 + 255) / 256)),
-                        dim3(256), 0, s, static_cast<const float*>(part), sp, B, I, bfp(l.act)));
-  // 10-11. down projection + residual(h1) -> out
-  sp = pick_splits(H, I, sms);
-  ENIGMA_TRY(splitk_gemm(bfp(l.act), d.w_down, part, B, H, I, sp, status, s));
-  ENIGMA_TRY(launch_pdl(reduce_residual_norm_kernel, dim3(B), dim3(256), 0, s,
-                        static_cast<const float*>(part), sp, B, H,
-                        static_cast<const __nv_bfloat16*>(bfp(l.h1)),
-                        static_cast<__nv_bfloat16*>(out),
-                        static_cast<const __nv_bfloat16*>(nullptr),
-                        static_cast<__nv_bfloat16*>(nullptr), 0.f));
+  // 4. O projection + residual(x) -> h1; h1 * w_post_norm -> h1w; row sums of h1^2 per tile
+  ea.ld = H;
+  ea.residual = static_cast<const __nv_bfloat16*>(x);
+  ea.h_out = bfp(l.h1);
+  ea.w_norm = static_cast<const __nv_bfloat16*>(d.w_post_norm);
+  ea.hw_out = bfp(l.h1w);
+  ea.ssq = reinterpret_cast<float*>(w + l.ssq);
+  ENIGMA_TRY((cluster_gemm<EPI_OPROJ, 1>(bfp(l.attn), d.w_o, B, H, int64_t(Hq) * D, H / 64, 0, ea,
+                                        sms, status, s)));
+  // 5. gate|up projection of h1w, scaled by the post-attention RMSNorm factor, SwiGLU -> act
+  //    (rmsnorm(h) w W = r (h w) W with r = 1 / sqrt(mean(h^2) + eps) per row)
+  ea.I = I;
+  ea.ssq_tiles = H / 64;
+  ea.eps = d.eps;
+  ea.act = bfp(l.act);
+  ENIGMA_TRY((cluster_gemm<EPI_GATEUP, 2>(bfp(l.h1w), d.w_gate_up, B, 2 * int64_t(I), H,
+                                         (I + 63) / 64, I, ea, sms, status, s)));
+  // 6. down projection + residual(h1) -> out
+  ea.residual = bfp(l.h1);
+  ea.h_out = static_cast<__nv_bfloat16*>(out);
+  ENIGMA_TRY((cluster_gemm<EPI_DOWN, 1>(bfp(l.act), d.w_down, B, H, I, H / 64, 0, ea, sms,
+                                       status, s)));
 #undef ENIGMA_TRY
   return cudaSuccess;
 }
 
 size_t decode_workspace_bytes(const enigma_decode_layer_desc& d) {
-  return plan(d, sm_count()).total;
+  return plan(d).total;
 }
 
 cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x, void* out,
@@ -432,7 +652,7 @@ extern "C" int32_t enigma_decode_layer_bf16_noalloc(const enigma_decode_layer_de
   NoAllocDevice* dev = nullptr;
   rc = noalloc_setup(&dev);
   if (rc != ENIGMA_OK) return rc;
-  const size_t need = enigma::plan(*desc, dev->sms).total;
+  const size_t need = enigma::plan(*desc).total;
   if (need > kNoAllocScratchBytes) {
     enigma::set_error("bad argument: decode noalloc: this step needs %zu bytes of scratch, more than "
               "the fixed %zu-byte array of the no-allocation entry point; use "

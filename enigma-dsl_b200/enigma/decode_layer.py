@@ -141,7 +141,7 @@ class DecodeLayer:
 
     def capture(self, x, out):
         """Record one step (fixed x / out buffers, current position) as a CUDA graph and
-        return a function that replays it: the step's 11 launches become one submission."""
+        return a function that replays it: the step's 6 launches become one submission."""
         import torch
         side = torch.cuda.Stream(device=x.device)
         side.wait_stream(torch.cuda.current_stream(x.device))
