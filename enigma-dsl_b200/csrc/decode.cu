@@ -75,15 +75,20 @@ struct EpiArgs {
 constexpr int CK_THREADS = 192;
 constexpr int CK_MAX_CLUSTER = 8;    // portable cluster size
 
-template <int NB>
+// The ring: STAGES A slots of AR rows (AR = 64 when M <= 64, else 128), then STAGES B slots.
+// The MMA always reads 128 A rows; with AR = 64 rows 64..127 of a slot are the next slot's
+// (or B slot 0's) bytes, which only feed accumulator rows >= M, never stored.  So a 64-row
+// slot halves the A bytes per stage and the same 96 KB holds more stages.
+template <int NB, int AR>
 struct CkShape {
-  static constexpr int STAGES = NB == 1 ? 4 : 3;
-  static constexpr int B_BYTES = NB * SK_BK * 64 * 2;              // 8 KB per 64 columns
-  static constexpr int STAGE = SK_A_BYTES + B_BYTES;
-  static constexpr int RING = STAGES * STAGE;                        // 96 KB
+  static constexpr int A_BYTES = AR * SK_BK * 2;                     // 8 or 16 KB
+  static constexpr int B_BYTES = NB * SK_BK * 64 * 2;                // 8 KB per 64 columns
+  static constexpr int STAGES = (96 * 1024) / (A_BYTES + B_BYTES);
+  static constexpr int RING = STAGES * (A_BYTES + B_BYTES);
   static constexpr int PSTRIDE = NB * 64 + 4;                        // floats per partial row
   static constexpr int SMEM = RING + 1024;
-  static_assert(SK_BM * PSTRIDE * 4 <= RING, "partial tile must fit in the drained ring");
+  static_assert(AR == 128 || B_BYTES >= 8192, "rows 64..127 of the last A slot must be in the ring");
+  static_assert(AR * PSTRIDE * 4 <= RING, "partial tile must fit in the drained ring");
 };
 
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
@@ -95,12 +100,39 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
 __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
   return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
-__device__ __forceinline__ float4 bf16x4_f4(const __nv_bfloat16* p) {
-  const uint2 r = *reinterpret_cast<const uint2*>(p);
-  return make_float4(bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y));
-}
 __device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float a, float b, float c, float d) {
   *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+}
+
+// Global inputs of one item's epilogue, loaded before the accumulator is complete.
+struct EpiIn {
+  float4 c0, c1, s0, s1;     // QKV: cos / sin at d.. and d + 32..
+  uint2 r, w;                // O-proj / down: residual; O-proj: norm weight
+};
+
+template <int EPI>
+__device__ __forceinline__ EpiIn ck_prefetch(const EpiArgs& e, int tile, int m, int g, bool valid) {
+  EpiIn in;
+  if constexpr (EPI == EPI_QKV) {
+    if (valid && g < 8 && tile < e.Hq + e.Hkv) {
+      const int d = 4 * g;
+      in.c0 = *reinterpret_cast<const float4*>(e.cosv + d);
+      in.c1 = *reinterpret_cast<const float4*>(e.cosv + d + 32);
+      in.s0 = *reinterpret_cast<const float4*>(e.sinv + d);
+      in.s1 = *reinterpret_cast<const float4*>(e.sinv + d + 32);
+    }
+  } else if constexpr (EPI == EPI_OPROJ || EPI == EPI_DOWN) {
+    if (valid) {
+      const int col = tile * 64 + 4 * g;
+      in.r = *reinterpret_cast<const uint2*>(e.residual + int64_t(m) * e.ld + col);
+      if constexpr (EPI == EPI_OPROJ) in.w = *reinterpret_cast<const uint2*>(e.w_norm + col);
+    }
+  }
+  return in;
+}
+
+__device__ __forceinline__ float4 bf16x4_u2(uint2 r) {
+  return make_float4(bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y));
 }
 
 // The epilogue of one item: row m, four columns 4 g.. of the tile (a0), and the matching
@@ -108,7 +140,8 @@ __device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float a, float b, fl
 // All threads call it (shuffles); `valid` marks a real item.
 template <int EPI>
 __device__ __forceinline__ void ck_epilogue(const EpiArgs& e, int tile, int m, int g, bool valid,
-                                            float4 a0, float4 a1, const float* s_rs) {
+                                            float4 a0, float4 a1, const EpiIn& in,
+                                            const float* s_rs) {
   if constexpr (EPI == EPI_QKV) {
     constexpr int D = 64, H2 = 32;
     if (!valid || g >= 8) return;
@@ -116,10 +149,14 @@ __device__ __forceinline__ void ck_epilogue(const EpiArgs& e, int tile, int m, i
     if (head >= e.Hq && head < e.Hq + e.Hkv && g == 0) e.counters[m * e.Hkv + head - e.Hq] = 0u;
     float lo[4] = {a0.x, a0.y, a0.z, a0.w}, hi[4] = {a1.x, a1.y, a1.z, a1.w};
     if (head < e.Hq + e.Hkv) {   // RoPE, rotate-half pairing d <-> d + 32
+      const float c0[4] = {in.c0.x, in.c0.y, in.c0.z, in.c0.w};
+      const float c1[4] = {in.c1.x, in.c1.y, in.c1.z, in.c1.w};
+      const float s0[4] = {in.s0.x, in.s0.y, in.s0.z, in.s0.w};
+      const float s1[4] = {in.s1.x, in.s1.y, in.s1.z, in.s1.w};
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        const float l2 = lo[t] * e.cosv[d + t] - hi[t] * e.sinv[d + t];
-        const float h2 = hi[t] * e.cosv[d + t + H2] + lo[t] * e.sinv[d + t + H2];
+        const float l2 = lo[t] * c0[t] - hi[t] * s0[t];
+        const float h2 = hi[t] * c1[t] + lo[t] * s1[t];
         lo[t] = l2;
         hi[t] = h2;
       }
@@ -139,10 +176,9 @@ __device__ __forceinline__ void ck_epilogue(const EpiArgs& e, int tile, int m, i
     float ss = 0.f;
     if (valid) {
       const int64_t o = int64_t(m) * e.ld + col;
-      const float4 r = bf16x4_f4(e.residual + o);
-      const float4 h = f4add(a0, r);
+      const float4 h = f4add(a0, bf16x4_u2(in.r));
       st_bf16x4(e.h_out + o, h.x, h.y, h.z, h.w);
-      const float4 w = bf16x4_f4(e.w_norm + col);
+      const float4 w = bf16x4_u2(in.w);
       st_bf16x4(e.hw_out + o, h.x * w.x, h.y * w.y, h.z * w.z, h.w * w.w);
       ss = h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
     }
@@ -162,25 +198,25 @@ __device__ __forceinline__ void ck_epilogue(const EpiArgs& e, int tile, int m, i
   } else {
     if (!valid) return;
     const int64_t o = int64_t(m) * e.ld + tile * 64 + 4 * g;
-    const float4 h = f4add(a0, bf16x4_f4(e.residual + o));
+    const float4 h = f4add(a0, bf16x4_u2(in.r));
     st_bf16x4(e.h_out + o, h.x, h.y, h.z, h.w);
   }
 }
 
 // Warp roles: warp 0 producer (one thread), warp 1 TMEM owner + MMA issuer (one thread),
 // warps 2..5 drain TMEM lanes 32 (warp % 4).. into the partial tile; then all six warps reduce.
-template <int EPI, int NB>
+template <int EPI, int NB, int AR>
 __global__ void __launch_bounds__(CK_THREADS)
 gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const EpiArgs ea, int num_kb, int a_rows, int b_col2, uint32_t* status) {
-  using S = CkShape<NB>;
+  using S = CkShape<NB, AR>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[S::STAGES], empty[S::STAGES], acc_full;
   __shared__ uint32_t tmem_slot;
   __shared__ float s_rs[SK_BM];           // EPI_GATEUP: RMSNorm factor of each row
   uint8_t* ring = align1024(smem_raw);
-  auto a_slot = [&](int s) { return ring + s * S::STAGE; };
-  auto b_slot = [&](int s) { return ring + s * S::STAGE + SK_A_BYTES; };
+  auto a_slot = [&](int s) { return ring + s * S::A_BYTES; };
+  auto b_slot = [&](int s) { return ring + S::STAGES * S::A_BYTES + s * S::B_BYTES; };
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x;
@@ -200,12 +236,8 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     tmem_alloc(&tmem_slot, NB * 64);
     tmem_relinquish();
   }
-  if (a_rows < SK_BM) {   // rows a_rows..127 of every A slot stay zero (TMA never writes them)
-    const int per = (SK_BM - a_rows) * 8;
-    for (int i = threadIdx.x; i < S::STAGES * per; i += CK_THREADS)
-      reinterpret_cast<uint4*>(a_slot(i / per) + a_rows * 128)[i % per] = make_uint4(0, 0, 0, 0);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
+  // A rows >= M are whatever the slot holds: accumulator rows are independent, and rows
+  // >= M are never stored.
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -229,6 +261,14 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
   }
   griddep_wait();   // A (the previous kernel's output) is ready
+  // This thread's first reduction item; its epilogue inputs are loaded now, while the
+  // MMAs run.
+  const int rows_per = (ea.M + cs - 1) / cs;
+  const int r0 = rank * rows_per;
+  const int r1 = min(ea.M, r0 + rows_per);
+  const EpiIn in0 = ck_prefetch<EPI>(ea, tile, r0 + int(threadIdx.x) / 16, int(threadIdx.x) % 16,
+                                     int(threadIdx.x) < rows_per * 16 &&
+                                         r0 + int(threadIdx.x) / 16 < r1);
   if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < pre; ++i) tma_load_2d(a_slot(i), &tmA, &full[i], (kb0 + i) * SK_BK, 0);
@@ -301,9 +341,6 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     tmem_dealloc(tmem, NB * 64);
   }
   cluster_sync();   // every CTA's partial tile is complete and visible to the cluster
-  const int rows_per = (ea.M + cs - 1) / cs;
-  const int r0 = rank * rows_per;
-  const int r1 = min(ea.M, r0 + rows_per);
   const uint32_t pbase = smem_u32(ring);
   const int iters = (rows_per * 16 + CK_THREADS - 1) / CK_THREADS;
   for (int itn = 0; itn < iters; ++itn) {
@@ -332,9 +369,12 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
       }
     }
-    ck_epilogue<EPI>(ea, tile, m, g, valid, a0, a1, s_rs);
+    ck_epilogue<EPI>(ea, tile, m, g, valid, a0, a1,
+                     itn == 0 ? in0 : ck_prefetch<EPI>(ea, tile, m, g, valid), s_rs);
   }
-  cluster_sync();   // peers have finished reading this CTA's partial tile
+  // Peers have finished reading this CTA's partial tile (their loads completed before
+  // they arrive); nothing of this CTA's global writes needs ordering, so a relaxed arrive.
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
 // Persistent split-KV attention: one producer + DA_WARPS consumer warps per CTA, CTA c of
@@ -446,17 +486,17 @@ Layout plan(const enigma_decode_layer_desc& d) {
 
 // C-tile columns [tile * 64, +64) of A [M, K] x Bw [K, n_cols] (and, NB = 2, columns
 // b_col2 + tile * 64 ..) with epilogue EPI, as one cluster launch.
-template <int EPI, int NB>
-cudaError_t cluster_gemm(const void* A, const void* Bw, int64_t M, int64_t n_cols, int64_t K,
+template <int EPI, int NB, int AR>
+cudaError_t cluster_gemm_ar(const void* A, const void* Bw, int64_t M, int64_t n_cols, int64_t K,
                          int64_t tiles, int b_col2, const EpiArgs& ea, int sms, uint32_t* status,
                          cudaStream_t s) {
-  using S = CkShape<NB>;
+  using S = CkShape<NB, AR>;
   CUtensorMap ta, tb;
   const int a_rows = int(std::min<int64_t>(SK_BM, (M + 7) / 8 * 8));
   if (!make_tmap_bf16_2d(&ta, A, M, K, K, SK_BK, uint32_t(a_rows)) ||
       !make_tmap_bf16_2d(&tb, Bw, K, n_cols, n_cols, 64, SK_BK))
     return cudaErrorInvalidValue;
-  auto kern = gemm_cluster_kernel<EPI, NB>;
+  auto kern = gemm_cluster_kernel<EPI, NB, AR>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
   if (e != cudaSuccess) return e;
   const int64_t kbs = (K + SK_BK - 1) / SK_BK;
@@ -476,6 +516,14 @@ cudaError_t cluster_gemm(const void* A, const void* Bw, int64_t M, int64_t n_col
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, ea, int(kbs), a_rows, b_col2, status);
+}
+
+template <int EPI, int NB>
+cudaError_t cluster_gemm(const void* A, const void* Bw, int64_t M, int64_t n_cols, int64_t K,
+                         int64_t tiles, int b_col2, const EpiArgs& ea, int sms, uint32_t* status,
+                         cudaStream_t s) {
+  return M <= 64 ? cluster_gemm_ar<EPI, NB, 64>(A, Bw, M, n_cols, K, tiles, b_col2, ea, sms, status, s)
+                 : cluster_gemm_ar<EPI, NB, 128>(A, Bw, M, n_cols, K, tiles, b_col2, ea, sms, status, s);
 }
 
 }  // namespace
