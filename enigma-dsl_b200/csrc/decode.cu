@@ -75,27 +75,29 @@ struct EpiArgs {
 constexpr int CK_THREADS = 192;
 constexpr int CK_MAX_CLUSTER = 8;    // portable cluster size
 
-// The ring: STAGES A slots of AR rows (AR = 64 when M <= 64, else 128), then STAGES B slots.
-// The MMA always reads 128 A rows; with AR = 64 rows 64..127 of a slot are the next slot's
-// (or B slot 0's) bytes, which only feed accumulator rows >= M, never stored.  So a 64-row
-// slot halves the A bytes per stage and the same 96 KB holds more stages.
+// Shared memory: `stages` A slots of AR rows (AR = 64 when M <= 64, else 128), `stages` B
+// slots, then the receive area.  The MMA always reads 128 A rows; with AR = 64 rows 64..127
+// of a slot are the next slot's (or B slot 0's) bytes, which only feed accumulator rows
+// >= M, never stored.  So a 64-row slot halves the A bytes per stage.
+// The receive area holds, for this CTA's R = ceil(M / cs) rows of the tile, the partial of
+// every CTA of the cluster: [cs][R][PSTRIDE] fp32.
+constexpr int CK_MAX_STAGES = 12;
+
 template <int NB, int AR>
 struct CkShape {
   static constexpr int A_BYTES = AR * SK_BK * 2;                     // 8 or 16 KB
   static constexpr int B_BYTES = NB * SK_BK * 64 * 2;                // 8 KB per 64 columns
-  static constexpr int STAGES = (96 * 1024) / (A_BYTES + B_BYTES);
-  static constexpr int RING = STAGES * (A_BYTES + B_BYTES);
+  static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int PSTRIDE = NB * 64 + 4;                        // floats per partial row
-  static constexpr int SMEM = RING + 1024;
   static_assert(AR == 128 || B_BYTES >= 8192, "rows 64..127 of the last A slot must be in the ring");
-  static_assert(AR * PSTRIDE * 4 <= RING, "partial tile must fit in the drained ring");
 };
 
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
-  return v;
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory to a (possibly remote)
+// CTA's shared memory of the cluster, counted on that CTA's mbarrier `mbar` when it lands.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes,
+                                                     uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "r"(src), "r"(bytes), "r"(mbar) : "memory");
 }
 __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
   return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
@@ -204,32 +206,40 @@ __device__ __forceinline__ void ck_epilogue(const EpiArgs& e, int tile, int m, i
 }
 
 // Warp roles: warp 0 producer (one thread), warp 1 TMEM owner + MMA issuer (one thread),
-// warps 2..5 drain TMEM lanes 32 (warp % 4).. into the partial tile; then all six warps reduce.
+// warps 2..5 drain TMEM lanes 32 (warp % 4).. (lane = tile row) and push each CTA's rows to
+// it; then all six warps reduce and apply the epilogue.
 template <int EPI, int NB, int AR>
 __global__ void __launch_bounds__(CK_THREADS)
 gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const EpiArgs ea, int num_kb, int a_rows, int b_col2, uint32_t* status) {
+                    const EpiArgs ea, int num_kb, int a_rows, int b_col2, int stages,
+                    uint32_t* status) {
   using S = CkShape<NB, AR>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[S::STAGES], empty[S::STAGES], acc_full;
+  __shared__ uint64_t full[CK_MAX_STAGES], empty[CK_MAX_STAGES], acc_full, recv_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ float s_rs[SK_BM];           // EPI_GATEUP: RMSNorm factor of each row
   uint8_t* ring = align1024(smem_raw);
   auto a_slot = [&](int s) { return ring + s * S::A_BYTES; };
-  auto b_slot = [&](int s) { return ring + S::STAGES * S::A_BYTES + s * S::B_BYTES; };
+  auto b_slot = [&](int s) { return ring + stages * S::A_BYTES + s * S::B_BYTES; };
+  float* recv = reinterpret_cast<float*>(ring + stages * S::STAGE);
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x;
   const int cs = int(gridDim.y), rank = int(cluster_ctarank());
   const int kb0 = rank * num_kb / cs, kb1 = (rank + 1) * num_kb / cs, nkb = kb1 - kb0;
+  const int R = (ea.M + cs - 1) / cs;                  // rows owned per CTA
+  const int r0 = rank * R;
+  const int rows_own = max(0, min(ea.M, r0 + R) - r0);
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    for (int s = 0; s < S::STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&acc_full, 1);
+    mbar_init(&recv_bar, 1);
+    mbar_arrive_expect_tx(&recv_bar, uint32_t(cs * rows_own * S::PSTRIDE * 4));
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -241,6 +251,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  cluster_sync();   // every CTA's receive barrier is initialised before any row is pushed
   const uint32_t tmem = tmem_slot;
   const uint32_t tx = uint32_t(a_rows * SK_BK * 2 + S::B_BYTES);
   auto load_b = [&](int s, int kb) {
@@ -249,7 +260,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   };
   // Weights never depend on the previous kernel: the first stages' tiles and an L2 prefetch
   // of the rest of the slice are issued before waiting on it.
-  const int pre = nkb < S::STAGES ? nkb : S::STAGES;
+  const int pre = nkb < stages ? nkb : stages;
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < pre; ++i) {
       mbar_arrive_expect_tx(&full[i], tx);
@@ -263,18 +274,14 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   griddep_wait();   // A (the previous kernel's output) is ready
   // This thread's first reduction item; its epilogue inputs are loaded now, while the
   // MMAs run.
-  const int rows_per = (ea.M + cs - 1) / cs;
-  const int r0 = rank * rows_per;
-  const int r1 = min(ea.M, r0 + rows_per);
   const EpiIn in0 = ck_prefetch<EPI>(ea, tile, r0 + int(threadIdx.x) / 16, int(threadIdx.x) % 16,
-                                     int(threadIdx.x) < rows_per * 16 &&
-                                         r0 + int(threadIdx.x) / 16 < r1);
+                                     int(threadIdx.x) < rows_own * 16);
   if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < pre; ++i) tma_load_2d(a_slot(i), &tmA, &full[i], (kb0 + i) * SK_BK, 0);
       for (int i = pre; i < nkb; ++i) {
-        const int s = i % S::STAGES;
-        if (!mbar_wait(&empty[s], ((i / S::STAGES) & 1) ^ 1, status)) break;
+        const int s = i % stages;
+        if (!mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, status)) break;
         mbar_arrive_expect_tx(&full[s], tx);
         tma_load_2d(a_slot(s), &tmA, &full[s], (kb0 + i) * SK_BK, 0);
         load_b(s, kb0 + i);
@@ -286,8 +293,8 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       constexpr uint32_t idesc = idesc_bf16_f32(SK_BM, NB * 64, false, true);
       bool ok = true;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % S::STAGES;
-        if (!mbar_wait(&full[s], (i / S::STAGES) & 1, status)) { ok = false; break; }
+        const int s = i % stages;
+        if (!mbar_wait(&full[s], (i / stages) & 1, status)) { ok = false; break; }
         tc_fence_after();
         const uint64_t da = smem_desc_sw128(smem_u32(a_slot(s)), 16, 1024);
         const uint64_t db = smem_desc_sw128(smem_u32(b_slot(s)), 8192, 1024);
@@ -301,7 +308,9 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
     __syncwarp();
   } else {
-    // Drain: TMEM lane = row; the ring is idle once the accumulator is complete.
+    // Drain row `row` of the accumulator into this CTA's idle ring ([M][PSTRIDE] fp32), then
+    // push rows [q R, (q + 1) R) to CTA q of the cluster, into slot [rank] of its receive
+    // area, with one bulk copy per CTA.
     const int q = warp & 3, row = q * 32 + lane;
     if constexpr (EPI == EPI_GATEUP) {   // while the MMAs run
       float t4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -333,6 +342,16 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                           __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
       }
     }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the copies
+    asm volatile("bar.sync 1, 128;" ::: "memory");                   // the four drain warps
+    if (warp == 2 && lane < cs) {
+      const int o = lane, n = max(0, min(ea.M, (o + 1) * R) - o * R);
+      if (n > 0)
+        bulk_copy_to_cluster(
+            mapa_shared(smem_u32(recv + rank * R * S::PSTRIDE), uint32_t(o)),
+            smem_u32(reinterpret_cast<float*>(ring) + o * R * S::PSTRIDE),
+            uint32_t(n * S::PSTRIDE * 4), mapa_shared(smem_u32(&recv_bar), uint32_t(o)));
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -340,41 +359,30 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     tc_fence_after();
     tmem_dealloc(tmem, NB * 64);
   }
-  cluster_sync();   // every CTA's partial tile is complete and visible to the cluster
-  const uint32_t pbase = smem_u32(ring);
-  const int iters = (rows_per * 16 + CK_THREADS - 1) / CK_THREADS;
+  // Every CTA's rows have arrived here; once all CTAs have arrived on the cluster barrier,
+  // no copy to or from any CTA is in flight, so the wait before exit keeps every ring and
+  // receive area alive as long as it is read or written.
+  mbar_wait(&recv_bar, 0, status);
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  const int iters = (R * 16 + CK_THREADS - 1) / CK_THREADS;
   for (int itn = 0; itn < iters; ++itn) {
     const int idx = itn * CK_THREADS + int(threadIdx.x);
-    const int m = r0 + idx / 16, g = idx % 16;
-    const bool valid = idx < rows_per * 16 && m < r1;
+    const int rl = idx / 16, g = idx % 16, m = r0 + rl;
+    const bool valid = rl < rows_own;
     float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
     if (valid) {
-      // All remote loads first, then the sums: each load is a cluster round trip.
-      const uint32_t off = pbase + uint32_t((m * S::PSTRIDE + 4 * g) * 4);
-      const uint32_t off2 = off + uint32_t((NB == 2 ? 64 : 32) * 4);
       const bool second = NB == 2 || (EPI == EPI_QKV && g < 8);
-      float4 v0[CK_MAX_CLUSTER], v1[CK_MAX_CLUSTER];
-#pragma unroll
-      for (int p = 0; p < CK_MAX_CLUSTER; ++p) {
-        if (p < cs) {
-          v0[p] = ld_dsmem_f4(mapa_shared(off, uint32_t(p)));
-          if (second) v1[p] = ld_dsmem_f4(mapa_shared(off2, uint32_t(p)));
-        }
-      }
-#pragma unroll
-      for (int p = 0; p < CK_MAX_CLUSTER; ++p) {
-        if (p < cs) {
-          a0 = f4add(a0, v0[p]);
-          if (second) a1 = f4add(a1, v1[p]);
-        }
+      const float* src = recv + rl * S::PSTRIDE + 4 * g;
+      for (int p = 0; p < cs; ++p) {
+        const float* sp = src + p * R * S::PSTRIDE;
+        a0 = f4add(a0, *reinterpret_cast<const float4*>(sp));
+        if (second) a1 = f4add(a1, *reinterpret_cast<const float4*>(sp + (NB == 2 ? 64 : 32)));
       }
     }
     ck_epilogue<EPI>(ea, tile, m, g, valid, a0, a1,
                      itn == 0 ? in0 : ck_prefetch<EPI>(ea, tile, m, g, valid), s_rs);
   }
-  // Peers have finished reading this CTA's partial tile (their loads completed before
-  // they arrive); nothing of this CTA's global writes needs ordering, so a relaxed arrive.
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
 // Persistent split-KV attention: one producer + DA_WARPS consumer warps per CTA, CTA c of
@@ -486,25 +494,42 @@ Layout plan(const enigma_decode_layer_desc& d) {
 
 // C-tile columns [tile * 64, +64) of A [M, K] x Bw [K, n_cols] (and, NB = 2, columns
 // b_col2 + tile * 64 ..) with epilogue EPI, as one cluster launch.
+// Shared memory per CTA when two CTAs must share an SM (more CTAs than SMs), else one.
+constexpr int kCkSmemTwoPerSm = 112 * 1024;
+constexpr int kCkSmemOnePerSm = 200 * 1024;
+
 template <int EPI, int NB, int AR>
 cudaError_t cluster_gemm_ar(const void* A, const void* Bw, int64_t M, int64_t n_cols, int64_t K,
-                         int64_t tiles, int b_col2, const EpiArgs& ea, int sms, uint32_t* status,
-                         cudaStream_t s) {
+                            int64_t tiles, int b_col2, const EpiArgs& ea, int sms,
+                            uint32_t* status, cudaStream_t s) {
   using S = CkShape<NB, AR>;
   CUtensorMap ta, tb;
   const int a_rows = int(std::min<int64_t>(SK_BM, (M + 7) / 8 * 8));
   if (!make_tmap_bf16_2d(&ta, A, M, K, K, SK_BK, uint32_t(a_rows)) ||
       !make_tmap_bf16_2d(&tb, Bw, K, n_cols, n_cols, 64, SK_BK))
     return cudaErrorInvalidValue;
-  auto kern = gemm_cluster_kernel<EPI, NB, AR>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
-  if (e != cudaSuccess) return e;
   const int64_t kbs = (K + SK_BK - 1) / SK_BK;
   const int cs = pick_cluster(tiles, kbs, sms);
+  const int64_t R = (M + cs - 1) / cs;
+  const int recv = int(cs * R * S::PSTRIDE * 4);
+  int budget = tiles * cs > sms ? kCkSmemTwoPerSm : kCkSmemOnePerSm;
+  int stages = (budget - 1024 - recv) / S::STAGE;
+  if (stages < 2) stages = (227 * 1024 - 1024 - recv) / S::STAGE;
+  // No more stages than the CTA has k-blocks: all of its weight tiles are then requested
+  // before the wait, and the CTA leaves room for the next kernel's CTAs.
+  stages = std::min<int>(stages, std::max<int64_t>(2, (kbs + cs - 1) / cs));
+  // The drained ring stages the whole partial tile.
+  stages = std::max<int>(stages, int((M * S::PSTRIDE * 4 + S::STAGE - 1) / S::STAGE));
+  stages = std::min(stages, CK_MAX_STAGES);
+  if (stages < 2) return cudaErrorInvalidValue;
+  const int smem = 1024 + stages * S::STAGE + recv;
+  auto kern = gemm_cluster_kernel<EPI, NB, AR>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(tiles), unsigned(cs));
   cfg.blockDim = dim3(CK_THREADS);
-  cfg.dynamicSmemBytes = S::SMEM;
+  cfg.dynamicSmemBytes = size_t(smem);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -515,7 +540,7 @@ cudaError_t cluster_gemm_ar(const void* A, const void* Bw, int64_t M, int64_t n_
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, ea, int(kbs), a_rows, b_col2, status);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, ea, int(kbs), a_rows, b_col2, stages, status);
 }
 
 template <int EPI, int NB>
