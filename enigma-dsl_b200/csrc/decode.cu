@@ -397,9 +397,11 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   __shared__ uint64_t full[DA_NST], empty[DA_NST];
   __shared__ float s_m[DA_WARPS][8], s_l[DA_WARPS][8];
   __shared__ uint32_t s_last;
+  __shared__ int64_t s_seg_unit[DA_MAX_SEGS];
+  __shared__ uint32_t s_seg_n[DA_MAX_SEGS];
   const AttnCtx cx{&tmK, &tmV, q, opart, mlpart, counters, out, Hq, Hkv, cap, L, S, units,
                    scale_log2, status, int(blockIdx.x), int(gridDim.x), align1024(smem_raw),
-                   full, empty, s_m, s_l, &s_last};
+                   full, empty, s_m, s_l, &s_last, s_seg_unit, s_seg_n};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmK);
