@@ -2,9 +2,9 @@
 qwen_fused megakernel, examples/qwen_megakernel.py:228-269).
 
 `DecodeLayer` owns bf16 weights and the KV cache as torch CUDA tensors and
-calls enigma_decode_layer_bf16: RMSNorm -> QKV (split-K tcgen05) -> RoPE +
-KV append -> split-KV attention -> O-proj + residual -> RMSNorm -> gate|up ->
-SwiGLU -> down + residual.  `qwen_fused`-style DSL kernels are recognised by
+calls enigma_decode_layer_bf16: RMSNorm -> QKV (cluster split-K tcgen05, RoPE +
+KV append in its epilogue) -> split-KV attention -> O-proj (+ residual, norm weight
+and row sums of squares) -> gate|up (RMSNorm factor, SwiGLU) -> down (+ residual).  `qwen_fused`-style DSL kernels are recognised by
 enigma.compile and bound here too (bind_from_trace).
 """
 from __future__ import annotations
