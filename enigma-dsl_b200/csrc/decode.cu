@@ -385,31 +385,48 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
-// Persistent split-KV attention: one producer + DA_WARPS consumer warps per CTA, CTA c of
-// gridDim.x takes chunk range c (see AttnCtx).
+// Split-KV attention: one producer + DA_WARPS consumer warps per CTA.  Flat mode (cl = 0):
+// persistent, CTA c of gridDim.x takes chunk range c of all units' chunks, partials merged
+// through global memory by each unit's last CTA.  Cluster mode (cl > 0, grid units x cl,
+// clusters of cl): the cl CTAs of a cluster split one unit's chunks and merge over
+// distributed shared memory.
 __global__ void __launch_bounds__(DA_THREADS)
 decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const __nv_bfloat16* __restrict__ q, float* __restrict__ opart,
                    float* __restrict__ mlpart, uint32_t* __restrict__ counters,
                    __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int cap, int L, int S,
-                   int units, float scale_log2, uint32_t* status) {
+                   int units, float scale_log2, int cl, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[DA_NST], empty[DA_NST];
+  __shared__ uint64_t full[DA_NST], empty[DA_NST], recv_bar;
   __shared__ float s_m[DA_WARPS][8], s_l[DA_WARPS][8];
   __shared__ uint32_t s_last;
   __shared__ int64_t s_seg_unit[DA_MAX_SEGS];
   __shared__ uint32_t s_seg_n[DA_MAX_SEGS];
+  const int rank = cl > 0 ? int(cluster_ctarank()) : 0;
+  int64_t cb, ce;
+  if (cl > 0) {
+    const int64_t unit = blockIdx.x / cl;
+    cb = unit * S + int64_t(rank) * S / cl;
+    ce = unit * S + int64_t(rank + 1) * S / cl;
+  } else {
+    cb = range_start(int64_t(S) * units, blockIdx.x, gridDim.x);
+    ce = range_start(int64_t(S) * units, blockIdx.x + 1, gridDim.x);
+  }
   const AttnCtx cx{&tmK, &tmV, q, opart, mlpart, counters, out, Hq, Hkv, cap, L, S, units,
-                   scale_log2, status, int(blockIdx.x), int(gridDim.x), align1024(smem_raw),
-                   full, empty, s_m, s_l, &s_last, s_seg_unit, s_seg_n};
+                   scale_log2, status, int(blockIdx.x), int(gridDim.x), cl, rank, cb, ce,
+                   align1024(smem_raw), &recv_bar, full, empty, s_m, s_l, &s_last, s_seg_unit,
+                   s_seg_n};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
     attn_init(cx);
+    mbar_init(&recv_bar, 1);
+    if (cl > 0 && rank == 0) mbar_arrive_expect_tx(&recv_bar, uint32_t((cl - 1) * DA_PART));
     fence_barrier_init();
   }
   __syncthreads();
+  if (cl > 0) cluster_sync();   // rank 0's receive barrier is initialised before any copy
   griddep_launch_dependents();
   if (warp == DA_WARPS) {
     if (lane == 0) {
@@ -419,10 +436,15 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
       griddep_wait();
       attn_produce_rest(cx, ci, i);
     }
-    return;
+    __syncwarp();
+  } else {
+    griddep_wait();   // q, the appended K / V rows and the counters are ready
+    attn_consumers<1>(cx, warp, lane, threadIdx.x);
   }
-  griddep_wait();   // q, the appended K / V rows and the counters are ready
-  attn_consumers<1>(cx, warp, lane, threadIdx.x);
+  // Cluster mode: rank 0 arrives once every copy into it has landed, so after the wait no
+  // copy out of any CTA's ring is still reading it.
+  if (cl > 0)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
 }  // namespace
@@ -587,7 +609,8 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
   ea.counters = reinterpret_cast<uint32_t*>(w + l.counters);
   ENIGMA_TRY((cluster_gemm<EPI_QKV, 1>(bfp(l.xn), d.w_qkv, B, Nqkv, H, Nqkv / 64, 0, ea, sms,
                                       status, s)));
-  // 3. attention over position + 1 keys (split-KV, combined by each unit's last CTA)
+  // 3. attention over position + 1 keys (split-KV: the CTAs of a unit merge over distributed
+  //    shared memory, or, flat ranges, through global memory by the unit's last CTA)
   {
     CUtensorMap tk, tv;
     const uint64_t rows = uint64_t(B) * Hkv * uint64_t(d.cache_capacity);
@@ -597,14 +620,37 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
     e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              DA_SMEM);   // per device, cheap: set on every call
     if (e != cudaSuccess) return e;
-    const int64_t chunks = int64_t(B) * Hkv * l.attn_splits;
-    const int ctas = int(std::min<int64_t>(chunks, int64_t(sms) * DA_CTAS_PER_SM));
-    ENIGMA_TRY(launch_pdl(decode_attn_kernel, dim3(ctas), dim3(DA_THREADS), DA_SMEM, s, tk, tv, static_cast<const __nv_bfloat16*>(bfp(l.q)),
-                          reinterpret_cast<float*>(w + l.opart),
-                          reinterpret_cast<float*>(w + l.mlpart),
-                          reinterpret_cast<uint32_t*>(w + l.counters), bfp(l.attn), Hq, Hkv,
-                          int(d.cache_capacity), int(d.position + 1), l.attn_splits, B * Hkv,
-                          d.attn_scale * 1.4426950408889634f, status));
+    // Cluster mode when the units can fill the SMs with k <= DA_CL_MAX CTAs each in one
+    // wave (k = the smallest power of two with units x k >= SMs); else flat ranges.
+    const int64_t units = int64_t(B) * Hkv;
+    int cl = 1;
+    while (cl < DA_CL_MAX && units * cl < sms) cl *= 2;
+    if (units * cl < sms || units * cl > int64_t(sms) * DA_CTAS_PER_SM || cl > l.attn_splits)
+      cl = 0;
+    const int64_t chunks = units * l.attn_splits;
+    const int ctas = cl > 0 ? int(units * cl)
+                            : int(std::min<int64_t>(chunks, int64_t(sms) * DA_CTAS_PER_SM));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(ctas));
+    cfg.blockDim = dim3(DA_THREADS);
+    cfg.dynamicSmemBytes = DA_SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = unsigned(cl > 0 ? cl : 1);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    ENIGMA_TRY(cudaLaunchKernelEx(&cfg, decode_attn_kernel, tk, tv,
+                                  static_cast<const __nv_bfloat16*>(bfp(l.q)),
+                                  reinterpret_cast<float*>(w + l.opart),
+                                  reinterpret_cast<float*>(w + l.mlpart),
+                                  reinterpret_cast<uint32_t*>(w + l.counters), bfp(l.attn), Hq,
+                                  Hkv, int(d.cache_capacity), int(d.position + 1), l.attn_splits,
+                                  B * Hkv, d.attn_scale * 1.4426950408889634f, cl, status));
   }
   // 4. O projection + residual(x) -> h1; h1 * w_post_norm -> h1w; row sums of h1^2 per tile
   ea.ld = H;

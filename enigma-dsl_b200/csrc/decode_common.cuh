@@ -58,7 +58,12 @@ constexpr int DA_NST = 3;
 constexpr int DA_TILE = DA_KEYS * DA_D * 2;        // 16 KB: one of K or V
 constexpr int DA_STAGE = 2 * DA_TILE;
 constexpr int DA_MERGE = DA_WARPS * 8 * DA_D * 4;  // 8 KB: warp partials, then the weights
-constexpr int DA_SMEM = DA_NST * DA_STAGE + DA_MERGE + 1024;
+// Cluster mode: a unit's k <= DA_CL_MAX CTAs merge over distributed shared memory; each
+// sends rank 0 one partial of DA_PART bytes ([8][D] fp32 O, then [8] (m, l) pairs).
+constexpr int DA_CL_MAX = 4;
+constexpr int DA_PART = 8 * DA_D * 4 + 8 * 2 * 4;
+constexpr int DA_RECV = (DA_CL_MAX - 1) * DA_PART;
+constexpr int DA_SMEM = DA_NST * DA_STAGE + DA_MERGE + DA_RECV + 1024;
 constexpr int DA_CTAS_PER_SM = 2;
 constexpr int DA_MAX_SEGS = 8;
 
@@ -123,8 +128,12 @@ struct AttnCtx {
   int Hq, Hkv, cap, L, S, units;
   float scale_log2;
   uint32_t* status;
-  int vc, nvc;
-  uint8_t* stages;          // DA_NST stages, then the DA_MERGE merge area; 1024-aligned
+  int vc, nvc;              // flat mode: range vc of nvc over all units' chunks
+  int cl, cl_rank;          // cluster mode (cl > 0): rank cl_rank of the unit's cl CTAs
+  int64_t cb, ce;           // this CTA's chunk range [cb, ce)
+  uint8_t* stages;          // DA_NST stages, the DA_MERGE merge area, the DA_RECV receive
+                            // area (cluster rank 0); 1024-aligned
+  uint64_t* recv_bar;       // cluster mode: rank 0's receive barrier
   uint64_t* full;           // [DA_NST]
   uint64_t* empty;          // [DA_NST]
   float (*s_m)[8];          // [DA_WARPS][8]
@@ -132,8 +141,8 @@ struct AttnCtx {
   uint32_t* s_last;         // bit k: this CTA completed recorded segment k's unit
   int64_t* s_seg_unit;      // [DA_MAX_SEGS] segments written, not yet counted
   uint32_t* s_seg_n;        // [DA_MAX_SEGS] their chunk counts
-  __device__ int64_t c_begin() const { return range_start(int64_t(S) * units, vc, nvc); }
-  __device__ int64_t c_end() const { return range_start(int64_t(S) * units, vc + 1, nvc); }
+  __device__ int64_t c_begin() const { return cb; }
+  __device__ int64_t c_end() const { return ce; }
 };
 
 __device__ inline void attn_init(const AttnCtx& c) {
@@ -178,6 +187,73 @@ __device__ inline void attn_produce_rest(const AttnCtx& c, int64_t ci, int i) {
   }
 }
 
+
+// Cluster mode, end of the CTA's range (one unit): the warps' partials (s_o, s_m, s_l) are
+// merged into this CTA's (m, l, O); ranks > 0 send theirs to rank 0 with one bulk copy
+// (from the idle ring), rank 0 waits for the cl - 1 copies on its receive barrier, merges in
+// rank order and writes the bf16 output.  G * D / 4 <= 128 items: one per thread.
+template <int BAR>
+__device__ inline void attn_cluster_merge(const AttnCtx& cx, int64_t unit, int G, int tid,
+                                          const float* s_o) {
+  const int gg = tid / (DA_D / 4), d = (tid % (DA_D / 4)) * 4;
+  const bool has = tid < G * (DA_D / 4);
+  float M = -INFINITY, den = 0.f;
+  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (has) {
+    M = cx.s_m[0][gg];                      // warp 0 always holds a valid key
+#pragma unroll
+    for (int w = 1; w < DA_WARPS; ++w) M = fmaxf(M, cx.s_m[w][gg]);
+#pragma unroll
+    for (int w = 0; w < DA_WARPS; ++w) {
+      const float wt = cx.s_m[w][gg] == -INFINITY ? 0.f : ex2f(cx.s_m[w][gg] - M);
+      const float4 v = *reinterpret_cast<const float4*>(s_o + (w * 8 + gg) * DA_D + d);
+      num.x = fmaf(wt, v.x, num.x);
+      num.y = fmaf(wt, v.y, num.y);
+      num.z = fmaf(wt, v.z, num.z);
+      num.w = fmaf(wt, v.w, num.w);
+      den = fmaf(wt, cx.s_l[w][gg], den);
+    }
+  }
+  float* recv = reinterpret_cast<float*>(cx.stages + DA_NST * DA_STAGE + DA_MERGE);
+  if (cx.cl_rank > 0) {
+    float* part = reinterpret_cast<float*>(cx.stages);   // the ring is idle
+    if (has) {
+      *reinterpret_cast<float4*>(part + gg * DA_D + d) = num;
+      if (d == 0) *reinterpret_cast<float2*>(part + 8 * DA_D + gg * 2) = make_float2(M, den);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the copy
+    consumers_sync<BAR>();
+    if (tid == 0) {
+      const uint32_t dst = mapa_shared(smem_u32(recv + (cx.cl_rank - 1) * (DA_PART / 4)), 0u);
+      const uint32_t bar = mapa_shared(smem_u32(cx.recv_bar), 0u);
+      asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"(dst), "r"(smem_u32(part)), "r"(uint32_t(DA_PART)), "r"(bar) : "memory");
+    }
+    return;
+  }
+  mbar_wait(cx.recv_bar, 0, cx.status);
+  if (!has) return;
+  float Mx = M;
+  for (int p = 0; p < cx.cl - 1; ++p) Mx = fmaxf(Mx, recv[p * (DA_PART / 4) + 8 * DA_D + gg * 2]);
+  const float c0 = ex2f(M - Mx);
+  num.x *= c0; num.y *= c0; num.z *= c0; num.w *= c0;
+  den *= c0;
+  for (int p = 0; p < cx.cl - 1; ++p) {
+    const float* pp = recv + p * (DA_PART / 4);
+    const float2 ml = *reinterpret_cast<const float2*>(pp + 8 * DA_D + gg * 2);
+    const float4 v = *reinterpret_cast<const float4*>(pp + gg * DA_D + d);
+    const float w = ex2f(ml.x - Mx);
+    num.x = fmaf(w, v.x, num.x);
+    num.y = fmaf(w, v.y, num.y);
+    num.z = fmaf(w, v.z, num.z);
+    num.w = fmaf(w, v.w, num.w);
+    den = fmaf(w, ml.y, den);
+  }
+  const float inv = 1.0f / den;
+  const int64_t b = int(unit) / cx.Hkv, kvh = int(unit) % cx.Hkv;
+  *reinterpret_cast<uint2*>(cx.out + (b * cx.Hq + kvh * G + gg) * DA_D + d) =
+      make_uint2(pack_bf16x2(num.x * inv, num.y * inv), pack_bf16x2(num.z * inv, num.w * inv));
+}
 
 // The DA_WARPS consumer warps of a group (warp 0..3 within the group, tid 0..127); BAR is
 // the group's named barrier.
@@ -312,6 +388,10 @@ __device__ inline void attn_consumers(const AttnCtx& cx, int warp, int lane, int
     }
     consumers_sync<BAR>();
     const int64_t pbase = (unit * cx.S + seg_first) * G;
+    if (cx.cl > 0) {   // one segment per CTA: merge over the cluster, then done
+      attn_cluster_merge<BAR>(cx, unit, G, tid, s_o);
+      return;
+    }
     for (int idx = tid; idx < G * (DA_D / 4); idx += DA_WARPS * 32) {
       const int gg = idx / (DA_D / 4), d = (idx % (DA_D / 4)) * 4;
       float M = cx.s_m[0][gg];                      // warp 0 always holds a valid key

@@ -30,7 +30,8 @@ def _run(cfg, seed=0):
     (2, 128, 2, 1, 256, 10, 74), (64, 896, 14, 2, 4864, 2048, 2112), (5, 512, 8, 2, 1024, 300, 364),
     (1, 1024, 16, 8, 3072, 32, 96),
     (128, 256, 4, 2, 512, 200, 264),     # the largest batch: a full 128-row A box
-    (3, 256, 4, 1, 512, 299, 300)])      # the appended key in the cache's last slot
+    (3, 256, 4, 1, 512, 299, 300),       # the appended key in the cache's last slot
+    (24, 256, 4, 2, 512, 600, 640)])     # 48 units: clusters of 4 CTAs per unit
 def test_decode_layer(cuda, batch, hidden, hq, hkv, inter, cache, cap):
     from enigma.decode_layer import DecodeConfig
     cfg = DecodeConfig(batch=batch, hidden=hidden, heads_q=hq, heads_kv=hkv, intermediate=inter,
