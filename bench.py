@@ -271,10 +271,10 @@ def _ops_side(hbm_peak, tc_peak, peak_kind):
         o = torch.empty_like(q)
         for causal in (True, False):
             fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
-            for _ in range(2):
+            for _ in range(3):
                 fn()
             with ClockSampler(torch.cuda.current_device()) as clk:
-                ms = _time_device(fn, 5, stream)
+                ms = _time_device(fn, 10, stream)
             fl = (2 if causal else 4) * B * H * S * S * D
             tf = fl / (ms * 1e-3) / 1e12
             res[f"sdpa_bf16_{'causal' if causal else 'noncausal'}_8x32x8192x128"] = {

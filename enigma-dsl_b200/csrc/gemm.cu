@@ -23,7 +23,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 
 #include "common.cuh"
 
@@ -479,7 +478,7 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
     cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    if (M >= 256 && N >= 256 && !(getenv("ENIGMA_GEMM_1SM") && getenv("ENIGMA_GEMM_1SM")[0] == '1')) {
+    if (M >= 256 && N >= 256) {
       // CTA-pair kernel: B boxes of the pair's two N halves, A boxes of 128 rows.
       const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
       const bool half = 2 * ptiles <= sm_count() / 2;
