@@ -394,8 +394,9 @@ __global__ void __launch_bounds__(DA_THREADS)
 decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const __nv_bfloat16* __restrict__ q, float* __restrict__ opart,
                    float* __restrict__ mlpart, uint32_t* __restrict__ counters,
-                   __nv_bfloat16* __restrict__ out, int Hq, int Hkv, int cap, int L, int S,
-                   int units, float scale_log2, int cl, uint32_t* status) {
+                   __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ kcache,
+                   const __nv_bfloat16* __restrict__ vcache, int Hq, int Hkv, int cap, int L,
+                   int S, int units, float scale_log2, int cl, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[DA_NST], empty[DA_NST], recv_bar;
   __shared__ float s_m[DA_WARPS][8], s_l[DA_WARPS][8];
@@ -405,14 +406,18 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   const int rank = cl > 0 ? int(cluster_ctarank()) : 0;
   int64_t cb, ce;
   if (cl > 0) {
+    // The chunks cover the L - 1 cached keys; the appended key joins in rank 0's merge, so
+    // the ranks split whole chunks evenly and no chunk is loaded for that one key.
     const int64_t unit = blockIdx.x / cl;
-    cb = unit * S + int64_t(rank) * S / cl;
-    ce = unit * S + int64_t(rank + 1) * S / cl;
+    const int sc = (L - 1 + DA_KEYS - 1) / DA_KEYS;
+    cb = unit * S + int64_t(rank) * sc / cl;
+    ce = unit * S + int64_t(rank + 1) * sc / cl;
+    L -= 1;
   } else {
     cb = range_start(int64_t(S) * units, blockIdx.x, gridDim.x);
     ce = range_start(int64_t(S) * units, blockIdx.x + 1, gridDim.x);
   }
-  const AttnCtx cx{&tmK, &tmV, q, opart, mlpart, counters, out, Hq, Hkv, cap, L, S, units,
+  const AttnCtx cx{&tmK, &tmV, q, opart, mlpart, counters, out, kcache, vcache, Hq, Hkv, cap, L, S, units,
                    scale_log2, status, int(blockIdx.x), int(gridDim.x), cl, rank, cb, ce,
                    align1024(smem_raw), &recv_bar, full, empty, s_m, s_l, &s_last, s_seg_unit,
                    s_seg_n};
@@ -625,7 +630,8 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
     const int64_t units = int64_t(B) * Hkv;
     int cl = 1;
     while (cl < DA_CL_MAX && units * cl < sms) cl *= 2;
-    if (units * cl < sms || units * cl > int64_t(sms) * DA_CTAS_PER_SM || cl > l.attn_splits)
+    const int cached_chunks = int((d.position + DA_KEYS - 1) / DA_KEYS);
+    if (units * cl < sms || units * cl > int64_t(sms) * DA_CTAS_PER_SM || cl > cached_chunks)
       cl = 0;
     const int64_t chunks = units * l.attn_splits;
     const int ctas = cl > 0 ? int(units * cl)
@@ -648,7 +654,9 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
                                   static_cast<const __nv_bfloat16*>(bfp(l.q)),
                                   reinterpret_cast<float*>(w + l.opart),
                                   reinterpret_cast<float*>(w + l.mlpart),
-                                  reinterpret_cast<uint32_t*>(w + l.counters), bfp(l.attn), Hq,
+                                  reinterpret_cast<uint32_t*>(w + l.counters), bfp(l.attn),
+                                  static_cast<const __nv_bfloat16*>(d.k_cache),
+                                  static_cast<const __nv_bfloat16*>(d.v_cache), Hq,
                                   Hkv, int(d.cache_capacity), int(d.position + 1), l.attn_splits,
                                   B * Hkv, d.attn_scale * 1.4426950408889634f, cl, status));
   }

@@ -125,7 +125,11 @@ struct AttnCtx {
   float* mlpart;
   uint32_t* counters;
   __nv_bfloat16* out;
-  int Hq, Hkv, cap, L, S, units;
+  const __nv_bfloat16* kcache;   // [units, cap, D] (cluster mode: the appended key's row)
+  const __nv_bfloat16* vcache;
+  int Hq, Hkv, cap;
+  int L;                    // keys the chunks cover (cluster mode: the cached ones, pos)
+  int S, units;             // S: chunk stride per unit
   float scale_log2;
   uint32_t* status;
   int vc, nvc;              // flat mode: range vc of nvc over all units' chunks
@@ -188,10 +192,11 @@ __device__ inline void attn_produce_rest(const AttnCtx& c, int64_t ci, int i) {
 }
 
 
-// Cluster mode, end of the CTA's range (one unit): the warps' partials (s_o, s_m, s_l) are
-// merged into this CTA's (m, l, O); ranks > 0 send theirs to rank 0 with one bulk copy
-// (from the idle ring), rank 0 waits for the cl - 1 copies on its receive barrier, merges in
-// rank order and writes the bf16 output.  G * D / 4 <= 128 items: one per thread.
+// Cluster mode, end of the CTA's range (one unit's cached keys): the warps' partials (s_o,
+// s_m, s_l) are merged into this CTA's (m, l, O); ranks > 0 send theirs to rank 0 with one
+// bulk copy (from the idle ring), rank 0 waits for the cl - 1 copies on its receive barrier,
+// merges them in rank order with the appended key and writes the bf16 output.
+// G * D / 4 <= 128 items: one per thread.
 template <int BAR>
 __device__ inline void attn_cluster_merge(const AttnCtx& cx, int64_t unit, int G, int tid,
                                           const float* s_o) {
@@ -232,8 +237,25 @@ __device__ inline void attn_cluster_merge(const AttnCtx& cx, int64_t unit, int G
     return;
   }
   mbar_wait(cx.recv_bar, 0, cx.status);
+  // The appended key (cache row cx.L of the unit) is one more partial: m = q.k in log2
+  // units, l = 1, O = v.  The 16 threads of head gg hold 4 dimensions each of the product.
+  const int64_t b = int(unit) / cx.Hkv, kvh = int(unit) % cx.Hkv;
+  float sn = 0.f;
+  float4 vn = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (has) {
+    const int64_t row = (unit * cx.cap + cx.L) * DA_D + d;
+    const uint2 qv = *reinterpret_cast<const uint2*>(cx.q + (b * cx.Hq + kvh * G + gg) * DA_D + d);
+    const uint2 kv = *reinterpret_cast<const uint2*>(cx.kcache + row);
+    const uint2 vv = *reinterpret_cast<const uint2*>(cx.vcache + row);
+    sn = bf16_lo(qv.x) * bf16_lo(kv.x) + bf16_hi(qv.x) * bf16_hi(kv.x) +
+         bf16_lo(qv.y) * bf16_lo(kv.y) + bf16_hi(qv.y) * bf16_hi(kv.y);
+    vn = make_float4(bf16_lo(vv.x), bf16_hi(vv.x), bf16_lo(vv.y), bf16_hi(vv.y));
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) sn += __shfl_xor_sync(0xffffffffu, sn, o);
+  sn *= cx.scale_log2;
   if (!has) return;
-  float Mx = M;
+  float Mx = fmaxf(M, sn);
   for (int p = 0; p < cx.cl - 1; ++p) Mx = fmaxf(Mx, recv[p * (DA_PART / 4) + 8 * DA_D + gg * 2]);
   const float c0 = ex2f(M - Mx);
   num.x *= c0; num.y *= c0; num.z *= c0; num.w *= c0;
@@ -249,8 +271,15 @@ __device__ inline void attn_cluster_merge(const AttnCtx& cx, int64_t unit, int G
     num.w = fmaf(w, v.w, num.w);
     den = fmaf(w, ml.y, den);
   }
+  {
+    const float w = ex2f(sn - Mx);
+    num.x = fmaf(w, vn.x, num.x);
+    num.y = fmaf(w, vn.y, num.y);
+    num.z = fmaf(w, vn.z, num.z);
+    num.w = fmaf(w, vn.w, num.w);
+    den += w;
+  }
   const float inv = 1.0f / den;
-  const int64_t b = int(unit) / cx.Hkv, kvh = int(unit) % cx.Hkv;
   *reinterpret_cast<uint2*>(cx.out + (b * cx.Hq + kvh * G + gg) * DA_D + d) =
       make_uint2(pack_bf16x2(num.x * inv, num.y * inv), pack_bf16x2(num.z * inv, num.w * inv));
 }
