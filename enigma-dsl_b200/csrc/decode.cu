@@ -363,6 +363,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   // no copy to or from any CTA is in flight, so the wait before exit keeps every ring and
   // receive area alive as long as it is read or written.
   mbar_wait(&recv_bar, 0, status);
+  __syncwarp();   // the .aligned cluster barrier needs converged warps
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   const int iters = (R * 16 + CK_THREADS - 1) / CK_THREADS;
   for (int itn = 0; itn < iters; ++itn) {
@@ -382,6 +383,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     ck_epilogue<EPI>(ea, tile, m, g, valid, a0, a1,
                      itn == 0 ? in0 : ck_prefetch<EPI>(ea, tile, m, g, valid), s_rs);
   }
+  __syncwarp();
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
@@ -448,8 +450,10 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   }
   // Cluster mode: rank 0 arrives once every copy into it has landed, so after the wait no
   // copy out of any CTA's ring is still reading it.
-  if (cl > 0)
+  if (cl > 0) {
+    __syncwarp();   // the .aligned cluster barrier needs converged warps
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+  }
 }
 
 }  // namespace
