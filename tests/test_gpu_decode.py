@@ -44,22 +44,26 @@ def test_decode_layer(cuda, batch, hidden, hq, hkv, inter, cache, cap):
     assert orc.rel_fro(kc, k_new) <= 5e-3 and orc.rel_fro(vc, v_new) <= 5e-3
 
 
-def test_decode_advance_two_tokens(cuda):
+@pytest.mark.parametrize("batch,hkv,cache,cap", [
+    (3, 2, 40, 64),        # 6 units: flat-range attention, global-memory merge
+    (64, 2, 300, 320)])    # 128 units: 2-CTA clusters per unit, DSMEM merge
+def test_decode_advance_two_tokens(cuda, batch, hkv, cache, cap):
     """Two steps with advance=True: the second attends over the first step's appended k/v."""
     import torch
     from enigma.decode_layer import DecodeConfig, DecodeLayer, rope_tables
-    cfg = DecodeConfig(batch=3, hidden=256, heads_q=4, heads_kv=2, intermediate=512,
-                       cache_len=40, cache_capacity=64)
+    cfg = DecodeConfig(batch=batch, hidden=256, heads_q=4, heads_kv=hkv, intermediate=512,
+                       cache_len=cache, cache_capacity=cap)
     layer = DecodeLayer.random(cfg, seed=3)
-    x1 = torch.randn(3, 256, device="cuda").bfloat16()
-    x2 = torch.randn(3, 256, device="cuda").bfloat16()
+    x1 = torch.randn(batch, 256, device="cuda").bfloat16()
+    x2 = torch.randn(batch, 256, device="cuda").bfloat16()
     layer.step(x1, advance=True)
     kc = layer.k_cache.float().cpu().numpy()
     vc = layer.v_cache.float().cpu().numpy()
     out = layer.step(x2).float().cpu().numpy()
-    c, s = rope_tables(cfg, 41)
+    c, s = rope_tables(cfg, cache + 1)
     w = {k: v.float().cpu().numpy() for k, v in layer.w.items()}
-    ref = orc.decode_layer(x2.float().cpu().numpy(), w, kc, vc, c, s, 41, 4, 2, 64, cfg.eps)[0]
+    ref = orc.decode_layer(x2.float().cpu().numpy(), w, kc, vc, c, s, cache + 1, 4, hkv, 64,
+                           cfg.eps)[0]
     assert orc.rel_fro(out, ref) <= 5e-3
 
 
@@ -73,12 +77,14 @@ def test_decode_rejects_bad_desc(cuda):
         layer.step(__import__("torch").zeros(2, 128, device="cuda").bfloat16())
 
 
-def test_decode_graph_replay_matches(cuda):
+@pytest.mark.parametrize("batch,hkv", [(8, 1), (64, 2)])
+def test_decode_graph_replay_matches(cuda, batch, hkv):
+    """A replayed CUDA graph gives the eager step's bits (every reduction has a fixed order)."""
     import torch
     from enigma.decode_layer import DecodeConfig, DecodeLayer
-    layer = DecodeLayer.random(DecodeConfig(batch=8, hidden=256, heads_q=4, heads_kv=1,
-                                            intermediate=512, cache_len=50, cache_capacity=64))
-    x = torch.randn(8, 256, device="cuda").bfloat16()
+    layer = DecodeLayer.random(DecodeConfig(batch=batch, hidden=256, heads_q=4, heads_kv=hkv,
+                                            intermediate=512, cache_len=300, cache_capacity=320))
+    x = torch.randn(batch, 256, device="cuda").bfloat16()
     eager = layer.step(x).float().cpu().numpy()
     out = torch.empty_like(x)
     replay = layer.capture(x, out)
