@@ -29,6 +29,7 @@ def _run(cfg, seed=0):
 @pytest.mark.parametrize("batch,hidden,hq,hkv,inter,cache,cap", [
     (2, 128, 2, 1, 256, 10, 74), (64, 896, 14, 2, 4864, 2048, 2112), (5, 512, 8, 2, 1024, 300, 364),
     (1, 1024, 16, 8, 3072, 32, 96),
+    (4, 128, 2, 1, 96, 10, 74),          # intermediate a multiple of 32, not of 64
     (128, 256, 4, 2, 512, 200, 264),     # the largest batch: a full 128-row A box
     (3, 256, 4, 1, 512, 299, 300),       # the appended key in the cache's last slot
     (24, 256, 4, 2, 512, 600, 640)])     # 48 units: clusters of 4 CTAs per unit
