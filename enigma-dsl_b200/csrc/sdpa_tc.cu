@@ -316,10 +316,12 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // Row max: four independent 3-input-max chains, then combined.
       float mq[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-      for (int k = 4; k < BN; k += 8) {
+      for (int k = 4; k + 8 <= BN; k += 8) {   // x[4 .. BN - 5]
 #pragma unroll
         for (int u = 0; u < 4; ++u) mq[u] = max3f(mq[u], x[k + u], x[k + 4 + u]);
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) mq[u] = fmaxf(mq[u], x[BN - 4 + u]);   // x[BN - 4 .. BN - 1]
       const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
       const float m_new = fmaxf(m_used, mx);
       // tcgen05.ld/st are warp-collective: the lazy-rescale decision is taken per warp.
