@@ -141,8 +141,11 @@ print(json.dumps(out))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("ENIGMA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("ENIGMA_REFERENCE"),
+                    help="root of the reference checkout (or set ENIGMA_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference (or ENIGMA_REFERENCE): the reference checkout to import")
     env = dict(os.environ, PYTHONPATH=a.reference, PYTHONDONTWRITEBYTECODE="1")
     r = subprocess.run([sys.executable, "-c", CHILD], env=env, capture_output=True, text=True,
                        cwd="/tmp")
