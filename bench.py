@@ -476,9 +476,11 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
-    if not args.no_ops:
+    # The per-operator lines and the CPU baseline are one-GPU figures: taken at N = 1 only
+    # (under torchrun the other GPUs would sit held while rank 0 measured them).
+    if not args.no_ops and world == 1:
         line["ops"] = _ops_side(hbm_peak, tc_peak, peak_kind)
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:
         line["cpu_baseline"] = _cpu_baseline(threads=1, sample_rows=args.cpu_rows)
     print(json.dumps(line), flush=True)
 
