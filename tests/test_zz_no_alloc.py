@@ -58,7 +58,7 @@ def test_noalloc_rejects_oversized_step(cuda):
     from enigma import _native
     layer = _layer(dict(batch=4, hidden=256, heads_q=4, heads_kv=2, intermediate=512,
                         cache_len=10, cache_capacity=16), seed=1)
-    layer.desc.intermediate = 1 << 22   # partials of the gate|up GEMM alone exceed 16 MiB
+    layer.desc.intermediate = 1 << 22   # the SwiGLU activations alone (4 x 2^22 bf16) exceed 16 MiB
     x = torch.zeros(4, 256, device="cuda").bfloat16()
     rc = _native.lib().enigma_decode_layer_bf16_noalloc(ctypes.byref(layer.desc), x.data_ptr(),
                                                         x.data_ptr(), None)
