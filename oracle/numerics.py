@@ -18,8 +18,14 @@ there are no stored golden arrays).  Parity pins:
                      enigma/ops/gemm.py:144-167 (C += A @ B).
   * decode layer     examples/qwen_megakernel.py:320-342 (full_decode_np), at the
                      BASELINE shapes; standard theta RoPE replaces the example's
-                     synthetic angles (unpinned, follows rope_np's half-split
-                     rotation at :313-317).
+                     synthetic angles (the rotation itself is rope_np's half-split
+                     form at :313-317).
+
+Pinning: tests/golden/numerics.npz holds outputs of the reference's own numpy
+code (extracted from the example scripts by tests/golden/make_numerics_golden.py
+and run on seeded inputs); tests/test_numerics_golden.py checks every function
+above against them.  Not pinned by any reference code: the causal mask and the
+theta-RoPE angle table (the rotation given the angles is pinned).
 """
 from __future__ import annotations
 
@@ -56,6 +62,15 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     ms = np.mean(x64 * x64, axis=-1, keepdims=True)
     y = x64 / np.sqrt(ms + eps) * np.asarray(w, dtype=np.float64)
     return y.astype(np.float32)
+
+
+def rmsnorm_fp32(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """The reference's own check written as it is, in fp32 end to end
+    (benchmark_rmsnorm.py:115-116: rms = sqrt(mean(X**2, axis=1) + EPS); (X / rms) * W).
+    This is the form the CPU baseline times; `rmsnorm` above is the (fp64) checker."""
+    x = np.asarray(x, dtype=np.float32)
+    rms = np.sqrt(np.mean(x ** 2, axis=-1, keepdims=True) + np.float32(eps))
+    return (x / rms) * np.asarray(w, dtype=np.float32)
 
 
 # --------------------------------------------------------------------------- GEMM
@@ -152,33 +167,46 @@ def rel_fro(a, b) -> float:
 
 
 # --------------------------------------------------------------------------- decode layer
+def rope(t, cos, sin):
+    """Half-split rotary embedding over the last axis (rope_np,
+    examples/qwen_megakernel.py:313-317): [lo, hi] -> [lo c - hi s, hi c + lo s] with the
+    first half of cos / sin applied to lo and the second half to hi.  fp64."""
+    t = np.asarray(t, np.float64)
+    cos = np.asarray(cos, np.float64)
+    sin = np.asarray(sin, np.float64)
+    half = t.shape[-1] // 2
+    lo, hi = t[..., :half], t[..., half:]
+    return np.concatenate([lo * cos[:half] - hi * sin[:half],
+                           hi * cos[half:] + lo * sin[half:]], axis=-1)
+
+
 def decode_layer(x, w, k_cache, v_cache, cos, sin, position, heads_q, heads_kv, head_dim,
-                 eps):
+                 eps, q_norm=None, k_norm=None):
     """One decode step, restating full_decode_np (examples/qwen_megakernel.py:320-342)
-    for a batch, bf16 weights given as fp32 arrays, no q/k head-norm.
+    for a batch, bf16 weights given as fp32 arrays.
 
     x [B, H]; k_cache / v_cache [B, Hkv, cap, D] with `position` valid entries (the new
     k, v are placed at `position`, the caches are not modified); cos / sin [D].
+    q_norm / k_norm [D] (optional) apply the Qwen3 per-head RMSNorm before RoPE
+    (qwen_megakernel.py:325-326); the BASELINE layer omits it (None).
     Returns (out [B, H], q_rot, k_new, v_new).  fp64 internally.
     """
     x = np.asarray(x, np.float64)
     f = {k: np.asarray(v, np.float64) for k, v in w.items()}
     B, H = x.shape
     D, G = head_dim, heads_q // heads_kv
-    half = D // 2
 
     def rms(v, wt):
         return v / np.sqrt(np.mean(v * v, axis=-1, keepdims=True) + eps) * wt
 
-    def rope(t):  # t [..., D]
-        lo, hi = t[..., :half], t[..., half:]
-        return np.concatenate([lo * cos[:half] - hi * sin[:half],
-                               hi * cos[half:] + lo * sin[half:]], axis=-1)
+    def head_norm(t, wt):
+        return t if wt is None else rms(t, np.asarray(wt, np.float64))
 
     xn = rms(x, f["w_in_norm"])
     qkv = xn @ f["w_qkv"]
-    q = rope(qkv[:, :heads_q * D].reshape(B, heads_q, D))
-    k = rope(qkv[:, heads_q * D:(heads_q + heads_kv) * D].reshape(B, heads_kv, D))
+    q = rope(head_norm(qkv[:, :heads_q * D].reshape(B, heads_q, D), q_norm), cos, sin)
+    k = rope(head_norm(qkv[:, heads_q * D:(heads_q + heads_kv) * D].reshape(B, heads_kv, D),
+                       k_norm), cos, sin)
     v = qkv[:, (heads_q + heads_kv) * D:].reshape(B, heads_kv, D)
     kc = np.asarray(k_cache[:, :, :position], np.float64)
     vc = np.asarray(v_cache[:, :, :position], np.float64)
