@@ -9,23 +9,25 @@ step.  Bytes per step are the algorithmic ones: read x once, write y once,
 read w once (4*rows*hidden + 2*hidden).  Inputs (4 GiB each way) are larger
 than the 126 MB L2, so no flush is needed between steps.
 
-With N > 1 (launched under torchrun, one rank per GPU) each rank processes
-its own full-size row shard (weak scaling, no collective on the data path);
-the timed region is bracketed by a barrier and cuda synchronize, and the
-elapsed time is the max over ranks.
+With N > 1 (launched under torchrun, one rank per GPU) the 262144 rows are
+split across the ranks (strong scaling, no collective on the data path); the
+timed region is bracketed by a barrier and cuda synchronize, the elapsed time
+is the max over ranks, and the NCCL all-gather of y is timed on its own.
 
 `ops` in the JSON line adds the other hot-path operators at their BASELINE
-headline sizes on rank 0 (GEMM bf16 8192^3, SDPA bf16 [8,32,8192,128]),
-TFLOP/s against the measured bf16 peak.
+headline sizes, sharded the same way across the ranks (GEMM bf16 8192^3 by
+M-blocks, SDPA bf16 [8,32,8192,128] by batch, the decode step by sequences),
+with the all-gather of each output timed separately.
 
 --impl reference times the reference's own CPU formulation of the same
-operator (the numpy check of examples/benchmark_rmsnorm.py:117-118, restated
-in oracle/numerics.py) on the host cores, on a bounded row sample per step.
+operator (the fp32 numpy check of examples/benchmark_rmsnorm.py:115-116) on
+all the host's cores, on a bounded row sample per step.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes
+import functools
 import json
 import math
 import os
@@ -41,9 +43,13 @@ sys.path.insert(0, str(ROOT / "enigma-dsl_b200"))
 ROWS, HIDDEN, EPS = 262144, 8192, 1e-6
 METRIC = "RMSNorm HBM GB/s (bf16 262144x8192, fp32 accumulate)"
 BYTES_PER_STEP = 4 * ROWS * HIDDEN + 2 * HIDDEN
-# DRAM bytes (read + write) of one rmsnorm launch at this size, from the ncu
-# capture summarised in profiles/rmsnorm_bf16_262144x8192.md (small case scaled x8).
-NCU_TRAFFIC_PER_LAUNCH = 8_192_407_552
+# DRAM bytes (read + write) per algorithmic byte of one rmsnorm launch, from an ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum) of a 32768 x 8192 launch, scaled
+# to the launch timed here by its bytes.  Writes still held in L2 when the kernel ends are
+# not in the capture, so it reads slightly below 1.
+NCU_TRAFFIC_PER_BYTE = 8_192_407_552 / 8_589_950_976
+NCU_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a 32768 x 8192 "
+                      "launch, scaled by bytes; excludes writes still in L2 at kernel end")
 
 
 def _set_rows(rows: int) -> None:
@@ -207,89 +213,166 @@ def _time_device_flushed(fn, steps, stream):
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def _cpu_rmsnorm_sample(sample_rows: int, threads: int):
-    """Time the oracle's numpy RMSNorm on `sample_rows` rows of the workload.
+def _host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
-    Returns (seconds, rows).  Rows are split across `threads` Python threads
-    (numpy releases the GIL inside its kernels).
-    """
+
+@functools.lru_cache(maxsize=2)
+def _cpu_inputs(sample_rows: int):
+    """Seeded bf16-rounded x [sample_rows, HIDDEN] and w, made once per size."""
     import numpy as np
-    from concurrent.futures import ThreadPoolExecutor
     from oracle import numerics as orc
     rng = np.random.default_rng(0)
     x = orc.bf16_round(rng.standard_normal((sample_rows, HIDDEN), dtype=np.float32))
     w = orc.bf16_round((1 + 0.1 * rng.standard_normal(HIDDEN)).astype(np.float32))
-    chunks = np.array_split(np.arange(sample_rows), threads)
+    return x, w
+
+
+def _cpu_rmsnorm_rate(sample_rows: int, threads: int, min_seconds: float, passes: int = 0):
+    """Time the reference's own RMSNorm formula (examples/benchmark_rmsnorm.py:115-116, fp32
+    numpy, as oracle/numerics.py:rmsnorm_fp32 writes it) over a `sample_rows`-row sample of
+    the workload, rows split across `threads` Python threads (numpy releases the GIL in its
+    kernels).  Repeats whole passes until `min_seconds` have elapsed (or `passes` passes).
+    Returns (seconds, rows processed)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import numerics as orc
+    x, w = _cpu_inputs(sample_rows)
+    chunks = [c for c in np.array_split(np.arange(sample_rows), threads * 4) if len(c)]
 
     def work(idx):
-        if len(idx):
-            orc.rmsnorm(x[idx[0]:idx[-1] + 1], w, EPS)
+        orc.rmsnorm_fp32(x[idx[0]:idx[-1] + 1], w, EPS)
 
-    t0 = time.perf_counter()
-    if threads == 1:
-        work(chunks[0])
-    else:
-        with ThreadPoolExecutor(threads) as ex:
+    done, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        while True:
             list(ex.map(work, chunks))
-    return time.perf_counter() - t0, sample_rows
+            done += sample_rows
+            el = time.perf_counter() - t0
+            if (passes and done >= passes * sample_rows) or (not passes and el >= min_seconds):
+                return el, done
 
 
-def _cpu_baseline(threads=1, sample_rows=16384):
-    dt, rows = _cpu_rmsnorm_sample(sample_rows, threads)
-    gbs = (4 * rows * HIDDEN + 2 * HIDDEN) / dt / 1e9
+def _cpu_sample_text(rows_done, dt, threads, sample_rows):
+    return (f"{rows_done} rows x {HIDDEN} in {dt:.1f} s ({threads} threads): repeated passes "
+            f"over a seeded {sample_rows}-row sample of the {ROWS}-row workload, the reference's fp32 "
+            f"numpy formula (examples/benchmark_rmsnorm.py:115-116) on bf16-rounded values; "
+            f"GB/s counts the workload's bf16 bytes (4 per element + w)")
+
+
+def _cpu_baseline(sample_rows=16384, min_seconds=10.0):
+    threads = _host_threads()
+    dt, rows = _cpu_rmsnorm_rate(sample_rows, threads, min_seconds)
+    gbs = (4 * rows * HIDDEN) / dt / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {ROWS} rows x {HIDDEN} (bf16-rounded inputs, fp64 numpy "
-                      f"oracle, oracle/numerics.py:rmsnorm), {dt:.2f} s"}
+            "sample": _cpu_sample_text(rows, dt, threads, sample_rows)}
+
+
+def _config(world: int) -> dict:
+    """The workload description both arms print (the same dict)."""
+    return {"workload": f"rmsnorm bf16 rows={ROWS} hidden={HIDDEN} eps={EPS}, rows sharded "
+                        f"across {world} GPU(s)",
+            "rows_total": ROWS, "hidden": HIDDEN, "parallelism": f"row-shard x{world}",
+            "l2": "inputs larger than L2 (126 MB) at every N; no flush",
+            "bytes_per_step_total": BYTES_PER_STEP}
 
 
 # ----------------------------------------------------------------------------- our arm
-def _ops_side(hbm_peak, tc_peak, peak_kind):
-    """GEMM / SDPA at their BASELINE headline sizes on this GPU (rank 0 only)."""
+def _timed_max(fn, steps, world, stream, flushed=False):
+    """Device ms per step of fn() on this rank (CUDA events on `stream`), bracketed by a
+    barrier and synchronize, and the max of that over ranks."""
     import torch
-    from enigma import cuda_ops
+    torch.cuda.synchronize()
+    _barrier(world)
+    ms = (_time_device_flushed if flushed else _time_device)(fn, steps, stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    return ms, _max_over_ranks(ms, world)
+
+
+def _allgather_ms(local, world, reps=3):
+    """NCCL all-gather of this rank's output shard into the full tensor on every rank,
+    timed alone (max over ranks); the only collective of the sharded path."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return None
+    full = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                       device=local.device)
+    dist.all_gather_into_tensor(full, local)
+    ms, ms_max = _timed_max(lambda: dist.all_gather_into_tensor(full, local), reps, world,
+                            torch.cuda.current_stream())
+    nbytes = full.numel() * full.element_size()
+    del full
+    # bus bandwidth convention of nccl-tests: (world-1)/world of the gathered bytes cross links
+    return {"ms": round(ms_max, 4), "bytes_gathered": nbytes,
+            "busbw_gbs": round(nbytes * (world - 1) / world / (ms_max * 1e-3) / 1e9, 1)}
+
+
+def _ops_side(world, rank, hbm_peak, tc_peak, peak_kind):
+    """GEMM, SDPA and the decode step at their BASELINE headline sizes, sharded the way
+    BASELINE configs 3-5 shard them: GEMM 8192^3 by M-blocks (B replicated, placed before
+    timing), SDPA [8,32,8192,128] by batch (whole (b, h) slices), decode batch 64 by
+    sequences (weights replicated).  Every rank runs its shard; the time is the max over
+    ranks and the value is the whole problem's work over that time.  At N = 1 these are
+    the single-GPU figures."""
+    import torch
+    from enigma import cuda_ops, shard
     res = {}
     stream = torch.cuda.current_stream()
     n = 8192
     g = torch.Generator(device="cuda").manual_seed(0)
-    a = (torch.randn(n, n, device="cuda", generator=g) / math.sqrt(n)).bfloat16()
+    lo, hi = shard.shard_range(n, world, rank)
+    a = (torch.randn(n, n, device="cuda", generator=g)[lo:hi] / math.sqrt(n)).bfloat16()
     b = torch.randn(n, n, device="cuda", generator=g).bfloat16()
-    c = torch.empty_like(a)
+    c = torch.empty(hi - lo, n, dtype=torch.bfloat16, device="cuda")
+    fn = lambda: cuda_ops.gemm(a, b, out=c)  # noqa: E731
     for _ in range(3):
-        cuda_ops.gemm(a, b, out=c)
+        fn()
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ms = _time_device(lambda: cuda_ops.gemm(a, b, out=c), 20, stream)
-    tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
-    res["gemm_bf16_8192"] = {"tflops": round(tf, 1), "ms": round(ms, 4),
-                             "frac": round(tf / tc_peak, 4), "peak": tc_peak,
-                             "peak_kind": peak_kind + " burst", "clocks": clk.summary()}
+        ms, ms_max = _timed_max(fn, 20, world, stream)
+    tf = 2 * n ** 3 / (ms_max * 1e-3) / 1e12
+    res["gemm_bf16_8192"] = {
+        "tflops": round(tf, 1), "ms": round(ms_max, 4), "n_gpus": world,
+        "rows_per_gpu": hi - lo, "frac": round(tf / world / tc_peak, 4), "peak": tc_peak,
+        "peak_kind": peak_kind + " burst, per GPU", "clocks": clk.summary(),
+        "allgather_C": _allgather_ms(c, world)}
     del a, b, c
-    if os.environ.get("ENIGMA_BENCH_SDPA", "1") == "1" and _sdpa_tc_available():
-        B, H, S, D = 8, 32, 8192, 128
-        q = torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()
-        k = torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()
-        v = torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()
-        o = torch.empty_like(q)
-        for causal in (True, False):
-            fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
-            for _ in range(3):
-                fn()
-            with ClockSampler(torch.cuda.current_device()) as clk:
-                ms = _time_device(fn, 10, stream)
-            fl = (2 if causal else 4) * B * H * S * S * D
-            tf = fl / (ms * 1e-3) / 1e12
-            res[f"sdpa_bf16_{'causal' if causal else 'noncausal'}_8x32x8192x128"] = {
-                "tflops": round(tf, 1), "ms": round(ms, 3), "frac": round(tf / tc_peak, 4),
-                "flops_convention": "causal 2*B*H*S^2*D, non-causal 4*B*H*S^2*D",
-                "clocks": clk.summary()}
-    res["decode_layer_config5"] = _decode_side(hbm_peak)
+    B, H, S, D = 8, 32, 8192, 128
+    blo, bhi = shard.shard_range(B, world, rank)
+    q, k, v = (torch.randn(bhi - blo, H, S, D, device="cuda", generator=g).bfloat16()
+               for _ in range(3))
+    o = torch.empty_like(q)
+    for causal in (True, False):
+        fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
+        for _ in range(3):
+            fn()
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            ms, ms_max = _timed_max(fn, 10, world, stream)
+        fl = (2 if causal else 4) * B * H * S * S * D
+        tf = fl / (ms_max * 1e-3) / 1e12
+        res[f"sdpa_bf16_{'causal' if causal else 'noncausal'}_8x32x8192x128"] = {
+            "tflops": round(tf, 1), "ms": round(ms_max, 3), "n_gpus": world,
+            "batch_per_gpu": bhi - blo, "frac": round(tf / world / tc_peak, 4),
+            "flops_convention": "causal 2*B*H*S^2*D, non-causal 4*B*H*S^2*D",
+            "clocks": clk.summary(),
+            "allgather_O": _allgather_ms(o, world) if not causal else None}
+    del q, k, v, o
+    res["decode_layer_config5"] = _decode_side(hbm_peak, world, rank)
     return res
 
 
-def _decode_side(hbm_peak):
-    """one decode step, batch 64, 2048-token KV cache (HBM-bound)."""
+def _decode_side(hbm_peak, world=1, rank=0):
+    """one decode step, batch 64 (split by sequences across ranks),
+    2048-token KV cache (HBM-bound)."""
     import torch
     from enigma.decode_layer import DecodeConfig, DecodeLayer
-    cfg = DecodeConfig()
+    full = DecodeConfig()
+    if world > 1:
+        from enigma import shard
+        cfg = shard.decode_shard_config(full)
+    else:
+        cfg = full
     layer = DecodeLayer.random(cfg, seed=0)
     x = torch.randn(cfg.batch, cfg.hidden, device="cuda").bfloat16()
     out = torch.empty_like(x)
@@ -297,17 +380,18 @@ def _decode_side(hbm_peak):
     fn = layer.capture(x, out)
     for _ in range(5):
         fn()
-    ms = _time_device_flushed(fn, 50, stream)
-    ms_warm = _time_device(fn, 50, stream)
+    _, ms = _timed_max(fn, 50, world, stream, flushed=True)
+    _, ms_warm = _timed_max(fn, 50, world, stream)
     kv = 2 * cfg.batch * cfg.heads_kv * (cfg.cache_len + 1) * cfg.head_dim * 2
-    byts = layer.weight_bytes() + kv
-    return {"ms": round(ms, 4), "tokens_per_s": round(cfg.batch / (ms * 1e-3), 1),
-            "algorithmic_bytes": byts, "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+    byts = layer.weight_bytes() + kv   # this rank's bytes per step
+    return {"ms": round(ms, 4), "tokens_per_s": round(full.batch / (ms * 1e-3), 1),
+            "n_gpus": world, "batch_per_gpu": cfg.batch,
+            "algorithmic_bytes_per_gpu": byts, "gbs_per_gpu": round(byts / (ms * 1e-3) / 1e9, 1),
             "frac_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm_peak, 4),
             "l2": "flushed (256 MB read) before every step",
             "ms_back_to_back": round(ms_warm, 4),
-            "note": "weights + KV read once per step; back to back, L2 (126 MB) can hold "
-                    "part of the 97 MB working set"}
+            "note": "weights (replicated) + this rank's KV read once per step; back to back, "
+                    "L2 (126 MB) can hold part of the 97 MB working set"}
 
 
 def _sdpa_tc_available() -> bool:
@@ -395,40 +479,39 @@ def run_sweep(args):
 
 def run_ours(args):
     import torch
-    from enigma import _native, cuda_ops
+    from enigma import _native, cuda_ops, shard
     rank, world, local = _dist_init(args.gpus)
     cuda_ops.ensure_device(torch.cuda.current_device())
     hbm_peak, tc_peak, peak_kind = _peaks()
     stream = torch.cuda.current_stream()
 
+    # Config 2's rows sharded across the ranks: each GPU normalises its own row range.
+    lo, hi = shard.shard_range(ROWS, world, rank)
+    rows_local = hi - lo
+    local_bytes = 4 * rows_local * HIDDEN + 2 * HIDDEN
     g = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    x = torch.randn(ROWS, HIDDEN, device="cuda", generator=g).bfloat16()
+    x = torch.randn(rows_local, HIDDEN, device="cuda", generator=g).bfloat16()
     w = (1 + 0.1 * torch.randn(HIDDEN, device="cuda", generator=g)).bfloat16()
     y = torch.empty_like(x)
     step = lambda: cuda_ops.rmsnorm(x, w, EPS, out=y)  # noqa: E731
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize()
-    _barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ms = _time_device(step, args.steps, stream)
-        torch.cuda.synchronize()
-    _barrier(world)
+        ms, ms_max = _timed_max(step, args.steps, world, stream)
     cuda_ops.synchronize(torch.cuda.current_device())
-    ms_max = _max_over_ranks(ms, world)
-    value = world * BYTES_PER_STEP / (ms_max * 1e-3) / 1e9
-    achieved = BYTES_PER_STEP / (ms * 1e-3) / 1e9  # one launch per step on this rank
+    value = BYTES_PER_STEP / (ms_max * 1e-3) / 1e9
+    achieved = local_bytes / (ms * 1e-3) / 1e9  # one launch per step on this rank
+    gather_y = _allgather_ms(y, world) if world > 1 else None
 
     # e2e through the C ABI with host buffers: enigma_rmsnorm_host takes pinned host x and w
-    # and writes host y, moving every row host -> device -> host each step in chunks whose
-    # uploads, kernels and downloads overlap on two streams.
+    # and writes host y, moving every row of this rank's shard host -> device -> host each
+    # step in chunks whose uploads, kernels and downloads overlap on two streams.
     lib = _native.lib()
-    nbytes = ROWS * HIDDEN * 2
+    nbytes = rows_local * HIDDEN * 2
     chunk = 8192
-    hx = torch.empty((ROWS, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
-    hy = torch.empty((ROWS, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
+    hx = torch.empty((rows_local, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
+    hy = torch.empty((rows_local, HIDDEN), dtype=torch.bfloat16, pin_memory=True)
     hw = torch.empty((HIDDEN,), dtype=torch.bfloat16, pin_memory=True)
     hx.copy_(x)
     hw.copy_(w)
@@ -440,76 +523,81 @@ def run_ours(args):
 
     def e2e_step():
         _native.check(lib.enigma_rmsnorm_host(_native.DTYPE_BF16, hx.data_ptr(), hw.data_ptr(),
-                                              hy.data_ptr(), ROWS, HIDDEN, EPS, ws.data_ptr(),
-                                              wsb.value, chunk, sp), "rmsnorm_host")
+                                              hy.data_ptr(), rows_local, HIDDEN, EPS,
+                                              ws.data_ptr(), wsb.value, chunk, sp), "rmsnorm_host")
 
     e2e_steps = max(3, min(args.steps, 10))
     for _ in range(2):
         e2e_step()
-    torch.cuda.synchronize()
-    _barrier(world)
-    e2e_ms = _max_over_ranks(_time_device(e2e_step, e2e_steps, stream), world)
-    e2e_value = world * BYTES_PER_STEP / (e2e_ms * 1e-3) / 1e9
-    del hx, hy, hw, ws
+    _, e2e_ms = _timed_max(e2e_step, e2e_steps, world, stream)
+    e2e_value = BYTES_PER_STEP / (e2e_ms * 1e-3) / 1e9
+    del hx, hy, hw, ws, x, y
 
+    ops = None if args.no_ops else _ops_side(world, rank, hbm_peak, tc_peak, peak_kind)
     if rank != 0:
         return
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (x ~ N(0,1), w ~ 1 + 0.1 N(0,1), torch generator seeded per rank)",
-        "config": {"workload": f"rmsnorm bf16 rows={ROWS} hidden={HIDDEN} eps={EPS} per GPU",
-                   "rows_per_gpu": ROWS, "hidden": HIDDEN, "parallelism": f"row-shard x{world}",
-                   "l2": "inputs (4 GiB) larger than L2; no flush",
-                   "bytes_per_step_per_gpu": BYTES_PER_STEP},
+        "config": _config(world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json hbm_gbs)",
-                     "traffic": NCU_TRAFFIC_PER_LAUNCH,
-                     "algorithmic_bytes_per_launch": BYTES_PER_STEP},
-        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s (algorithmic bytes / e2e time)",
+                     "traffic": round(NCU_TRAFFIC_PER_BYTE * local_bytes),
+                     "traffic_source": NCU_TRAFFIC_SOURCE,
+                     "algorithmic_bytes_per_launch": local_bytes,
+                     "rows_per_launch": rows_local},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": nbytes + HIDDEN * 2, "d2h_bytes_per_step": nbytes,
                 "ms_per_step": round(e2e_ms, 3),
-                "path": "C ABI enigma_rmsnorm_host: pinned host in / out, 8192-row chunks, "
-                        "uploads / kernels / downloads overlapped on two streams"},
+                "path": "C ABI enigma_rmsnorm_host per rank: pinned host in / out, 8192-row "
+                        "chunks, uploads / kernels / downloads overlapped on two streams; "
+                        "value = all ranks' algorithmic bytes / max e2e time; bytes per step "
+                        "are rank 0's"},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
-    # The per-operator lines and the CPU baseline are one-GPU figures: taken at N = 1 only
-    # (under torchrun the other GPUs would sit held while rank 0 measured them).
-    if not args.no_ops and world == 1:
-        line["ops"] = _ops_side(hbm_peak, tc_peak, peak_kind)
+    if gather_y is not None:
+        line["allgather_y"] = gather_y
+    if ops is not None:
+        line["ops"] = ops
+    # The CPU baseline is a one-host figure: taken at N = 1 only.
     if not args.no_cpu and world == 1:
-        line["cpu_baseline"] = _cpu_baseline(threads=1, sample_rows=args.cpu_rows)
+        line["cpu_baseline"] = _cpu_baseline(sample_rows=args.cpu_rows)
     print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
+    """The reference's CPU implementation of the path, timed on this host's cores: its fp32
+    numpy RMSNorm (examples/benchmark_rmsnorm.py:115-116; the reference's kernels are
+    Apple-Metal only).  Rank 0 alone runs under torchrun; the host is one machine at every
+    N, so the value does not grow with n_gpus."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    threads = _host_threads()
     sample = args.cpu_rows
-    for _ in range(args.warmup):
-        _cpu_rmsnorm_sample(min(sample, 1024), threads)
-    times = []
+    _cpu_rmsnorm_rate(sample, threads, 0.0, passes=args.warmup)
+    times, rows = [], 0
     for _ in range(args.steps):
-        dt, rows = _cpu_rmsnorm_sample(sample, threads)
+        dt, r = _cpu_rmsnorm_rate(sample, threads, 0.0, passes=1)
         times.append(dt)
-    dt = sum(times) / len(times)
-    gbs = (4 * sample * HIDDEN + 2 * HIDDEN) / dt / 1e9
+        rows += r
+    total = sum(times)
+    gbs = 4 * rows * HIDDEN / total / 1e9
     cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-           "sample": f"{sample} of {ROWS} rows x {HIDDEN} per step (numpy restatement of "
-                     "examples/benchmark_rmsnorm.py:117-118 in oracle/numerics.py)"}
+           "sample": _cpu_sample_text(rows, total, threads, sample)}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"rmsnorm bf16 rows={ROWS} hidden={HIDDEN} eps={EPS} per GPU",
-                   "note": "reference is Apple-Metal only; its CPU numpy formulation is timed"},
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / len(times) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": _config(world),
+        "host_note": "one host's cores at every n_gpus (the reference has no multi-device path)",
         "cpu_baseline": cpu,
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

@@ -12,8 +12,17 @@ namespace enigma {
 // SM count of the current device (cached per device).
 int sm_count();
 
-// Device word that bounded waits set on timeout (one per device, zeroed at init).
+// Device word that bounded waits set on timeout (one per device, zeroed at init; created
+// by the first call, nullptr if that allocation fails).
 uint32_t* device_status();
+// The same word if it already exists on the current device, else nullptr (never allocates).
+uint32_t* device_status_if_exists();
+// Reads and clears the no-allocation decode entry's status word on the current device
+// (0 if that entry has not run there).  Allocates nothing.
+cudaError_t noalloc_take_status(uint32_t* value);
+// One CTA that waits on a barrier nothing arrives on, gives up after `polls` polls and
+// flags *status as a timed-out bounded wait does.
+cudaError_t launch_timeout_probe(uint32_t* status, long long polls, cudaStream_t s);
 
 // Operator launchers (asynchronous).  Arguments are validated by the C ABI layer.
 cudaStream_t aux_stream();
@@ -48,6 +57,10 @@ cudaError_t qwen_decode_f32_launch(const enigma_qwen_decode_f32_desc& q, cudaStr
 
 cudaError_t elementwise_launch(int op, int dtype, const void* a, const void* b, void* c, int64_t n,
                                cudaStream_t s);
+
+// Records the name of the device kernel an operator launcher chose, for
+// enigma_last_kernel on the calling thread (a static string).
+void note_kernel(const char* name);
 
 // Records a message for enigma_last_error on the calling thread.
 void set_error(const char* fmt, ...);

@@ -696,7 +696,9 @@ size_t decode_workspace_bytes(const enigma_decode_layer_desc& d) {
 
 cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x, void* out,
                                 void* ws, cudaStream_t s) {
-  return decode_layer_run(d, x, out, ws, sm_count(), device_status(), s);
+  uint32_t* status = device_status();
+  if (status == nullptr) return cudaErrorMemoryAllocation;   // the kernels' waits need it
+  return decode_layer_run(d, x, out, ws, sm_count(), status, s);
 }
 
 }  // namespace enigma
@@ -712,7 +714,9 @@ cudaError_t decode_layer_launch(const enigma_decode_layer_desc& d, const void* x
 // The array costs kNoAllocScratchBytes on every GPU that loads the library, until the
 // process exits.  All calls share it and it keeps the previous call's contents: every
 // byte a step reads from it is written earlier in the same step, so nothing needs
-// clearing except the status word, which is zeroed at the start of each call.  Calls
+// clearing.  The entry has its own status word, also a static device array: a bounded
+// wait that runs out flags it, and enigma_synchronize / enigma_take_device_status report
+// it once (ENIGMA_ERR_TIMEOUT) and clear it, like the library's per-device word.  Calls
 // that overlap on the GPU (different streams, or different host threads on one device)
 // race on the array; serialize them on one stream.
 namespace {
@@ -794,11 +798,46 @@ extern "C" int32_t enigma_decode_layer_bf16_noalloc(const enigma_decode_layer_de
     return ENIGMA_ERR_BADARG;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(dev->status, 0, sizeof(uint32_t), s);
-  if (e == cudaSuccess)
-    e = enigma::decode_layer_run(*desc, x, out, dev->scratch, dev->sms, dev->status, s);
+  cudaError_t e = enigma::decode_layer_run(*desc, x, out, dev->scratch, dev->sms, dev->status, s);
   if (e != cudaSuccess) {
     enigma::set_error("decode noalloc launch failed: %s (%s)", cudaGetErrorName(e), cudaGetErrorString(e));
+    return ENIGMA_ERR_LAUNCH;
+  }
+  return ENIGMA_OK;
+}
+
+namespace enigma {
+cudaError_t noalloc_take_status(uint32_t* value) {
+  *value = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return e;
+  uint32_t* st = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_dev[dev].ready) st = g_noalloc_dev[dev].status;
+  }
+  if (st == nullptr) return cudaSuccess;
+  e = cudaMemcpy(value, st, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && *value != 0) e = cudaMemset(st, 0, sizeof(uint32_t));
+  return e;
+}
+}  // namespace enigma
+
+// Self-test of the no-allocation entry's timeout reporting: the same probe as
+// enigma_check_timeout_path, aimed at this entry's static status word.
+extern "C" int32_t enigma_decode_noalloc_check_timeout_path(int64_t polls, void* stream) {
+  if (polls < 0 || polls > (int64_t(1) << 24)) {
+    enigma::set_error("bad argument: polls must be in [0, 2^24]");
+    return ENIGMA_ERR_BADARG;
+  }
+  NoAllocDevice* dev = nullptr;
+  int32_t rc = noalloc_setup(&dev);
+  if (rc != ENIGMA_OK) return rc;
+  cudaError_t e = enigma::launch_timeout_probe(dev->status, static_cast<long long>(polls),
+                                               static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    enigma::set_error("timeout probe: %s", cudaGetErrorString(e));
     return ENIGMA_ERR_LAUNCH;
   }
   return ENIGMA_OK;

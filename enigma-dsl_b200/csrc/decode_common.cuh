@@ -236,7 +236,14 @@ __device__ inline void attn_cluster_merge(const AttnCtx& cx, int64_t unit, int G
     }
     return;
   }
-  mbar_wait(cx.recv_bar, 0, cx.status);
+  // Warp-uniform outcome: the shuffles below need every lane of the warp.
+  if (!__all_sync(0xffffffffu, mbar_wait(cx.recv_bar, 0, cx.status))) {
+    // A peer's partial never arrived (the status word is flagged).  Skip the merge and the
+    // store, and give copies still landing in this CTA's shared memory one more bounded
+    // wait before the CTA moves on to the final cluster barrier and exits.
+    mbar_wait(cx.recv_bar, 0, cx.status);
+    return;
+  }
   // The appended key (cache row cx.L of the unit) is one more partial: m = q.k in log2
   // units, l = 1, O = v.  The 16 threads of head gg hold 4 dimensions each of the product.
   const int64_t b = int(unit) / cx.Hkv, kvh = int(unit) % cx.Hkv;

@@ -471,6 +471,8 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
                       (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(B) % 16 == 0);
   if (tma_ok) {
+    uint32_t* status = device_status();
+    if (status == nullptr) return cudaErrorMemoryAllocation;   // the bounded waits need it
     CUtensorMap ta, tb;
     if (!make_tmap_bf16_2d(&ta, A, M, K, K, BK, BM) || !make_tmap_bf16_2d(&tb, B, K, N, N, 64, BK))
       return cudaErrorInvalidValue;
@@ -483,20 +485,23 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
       const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
       const bool half = 2 * ptiles <= sm_count() / 2;
       auto kern = half ? gemm_bf16_pair_kernel<true> : gemm_bf16_pair_kernel<false>;
+      note_kernel("gemm_bf16_pair_kernel");
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
       if (e != cudaSuccess) return e;
       const int pairs = int(std::min<int64_t>(half ? 2 * ptiles : ptiles, sm_count() / 2));
       kern<<<2 * pairs, THREADS, P_SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), int(M),
-                                              int(N), int(K), device_status());
+                                              int(N), int(K), status);
       return cudaGetLastError();
     }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = int(tiles < sm_count() ? tiles : sm_count());
+    note_kernel("gemm_bf16_tc_kernel");
     gemm_bf16_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(
-        ta, tb, static_cast<__nv_bfloat16*>(C), int(M), int(N), int(K), device_status());
+        ta, tb, static_cast<__nv_bfloat16*>(C), int(M), int(N), int(K), status);
     return cudaGetLastError();
   }
   dim3 grid(unsigned((N + 15) / 16), unsigned((M + 15) / 16));
+  note_kernel("gemm_simt_kernel");
   gemm_simt_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B),
       static_cast<__nv_bfloat16*>(C), int(M), int(N), int(K), 0);
@@ -506,6 +511,7 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
 cudaError_t gemm_f32_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
                             int64_t K, bool accumulate, cudaStream_t s) {
   dim3 grid(unsigned((N + 15) / 16), unsigned((M + 15) / 16));
+  note_kernel("gemm_simt_kernel");
   gemm_simt_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(A),
                                                static_cast<const float*>(B),
                                                static_cast<float*>(C), int(M), int(N), int(K),

@@ -280,8 +280,15 @@ int32_t enigma_qwen_decode_f32(const enigma_qwen_decode_f32_desc* d, void* strea
 int32_t enigma_dispatch(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
                         const int64_t* ip, int32_t n_ip, const float* fp, int32_t n_fp,
                         const uint32_t* grid3, const uint32_t* threads3, void* stream) {
-  (void)grid3;
-  (void)threads3;
+  // grid / threads are the Metal-style totals a caller of the reference passes; the
+  // operators pick their own CTA shapes, so they are only checked (NULL means "not given").
+  for (int i = 0; i < 3; ++i) {
+    if (grid3 != nullptr && grid3[i] == 0) return bad("dispatch: grid has a zero extent");
+    if (threads3 != nullptr && threads3[i] == 0) return bad("dispatch: threads has a zero extent");
+  }
+  if (threads3 != nullptr &&
+      uint64_t(threads3[0]) * threads3[1] * threads3[2] > 1024)
+    return bad("dispatch: threads per threadgroup exceed 1024");
   if (n_buffers > 0 && buffers == nullptr) return bad("dispatch: buffers is NULL");
   if (n_ip > 0 && ip == nullptr) return bad("dispatch: iparams is NULL");
   if (n_fp > 0 && fp == nullptr) return bad("dispatch: fparams is NULL");

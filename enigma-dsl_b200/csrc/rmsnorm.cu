@@ -166,6 +166,7 @@ cudaError_t launch_row(const void* x, const void* w, void* y, int64_t rows, int6
   // Enough CTAs to fill every SM several times over; each CTA strides over rows.
   const int64_t max_ctas = int64_t(sms) * (2048 / THREADS) * 8;
   const int grid = int(rows < max_ctas ? rows : max_ctas);
+  enigma::note_kernel("rmsnorm_row_kernel");
   rmsnorm_row_kernel<T, THREADS, NV, PRED><<<grid, THREADS, 0, s>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), static_cast<T*>(y), rows,
       1.0f / float(hidden), eps, int(hidden / Vec<T>::kElems));
@@ -201,6 +202,7 @@ cudaError_t dispatch(const void* x, const void* w, void* y, int64_t rows, int64_
   }
   const int64_t max_ctas = int64_t(sms) * 16;
   const int grid = int(rows < max_ctas ? rows : max_ctas);
+  enigma::note_kernel("rmsnorm_generic_kernel");
   rmsnorm_generic_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x),
                                                  static_cast<const T*>(w), static_cast<T*>(y),
                                                  rows, hidden, eps);

@@ -48,6 +48,10 @@ cudaError_t ensure_device_state(int dev) {
 }
 }  // namespace
 
+thread_local const char* g_last_kernel = "";
+
+void note_kernel(const char* name) { g_last_kernel = name; }
+
 void set_error(const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -64,6 +68,13 @@ int sm_count() {
 uint32_t* device_status() {
   const int d = current_device();
   if (ensure_device_state(d) != cudaSuccess) return nullptr;
+  return g_status[d];
+}
+
+uint32_t* device_status_if_exists() {
+  const int d = current_device();
+  if (d < 0 || d >= kMaxDev) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
   return g_status[d];
 }
 
@@ -94,6 +105,13 @@ __global__ void timeout_probe_kernel(uint32_t* status, long long polls) {
   atomicExch(status, enigma_sm100::kDevTimeout);
 }
 }  // namespace
+
+namespace enigma {
+cudaError_t launch_timeout_probe(uint32_t* status, long long polls, cudaStream_t s) {
+  timeout_probe_kernel<<<1, 32, 0, s>>>(status, polls);
+  return cudaGetLastError();
+}
+}  // namespace enigma
 
 using enigma::set_error;
 
@@ -150,6 +168,12 @@ int32_t enigma_last_error(char* buf, size_t len) {
   return ENIGMA_OK;
 }
 
+int32_t enigma_last_kernel(char* buf, size_t len) {
+  if (buf == nullptr || len == 0) return ENIGMA_ERR_BADARG;
+  snprintf(buf, len, "%s", enigma::g_last_kernel);
+  return ENIGMA_OK;
+}
+
 int32_t enigma_device_count(int32_t* count) {
   if (count == nullptr) return badarg("count is NULL");
   int n = 0;
@@ -197,13 +221,19 @@ int32_t enigma_stream_destroy(void* stream) {
 }
 
 int32_t enigma_take_device_status(int32_t* timeouts) {
-  uint32_t* st = enigma::device_status();
-  if (st == nullptr) return cuda_status(cudaErrorNoDevice, "device status");
+  // Reads (and clears) the status words that exist on the current device: the library's
+  // per-device word and the no-allocation decode entry's static word.  Neither is created
+  // here, so this call allocates nothing.
   uint32_t v = 0;
-  cudaError_t e = cudaMemcpy(&v, st, sizeof(v), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_status(e, "read device status");
-  if (v != 0) cudaMemset(st, 0, sizeof(uint32_t));
-  if (timeouts) *timeouts = static_cast<int32_t>(v);
+  if (uint32_t* st = enigma::device_status_if_exists()) {
+    cudaError_t e = cudaMemcpy(&v, st, sizeof(v), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_status(e, "read device status");
+    if (v != 0) cudaMemset(st, 0, sizeof(uint32_t));
+  }
+  uint32_t w = 0;
+  cudaError_t e = enigma::noalloc_take_status(&w);
+  if (e != cudaSuccess) return cuda_status(e, "read no-allocation status");
+  if (timeouts) *timeouts = static_cast<int32_t>(v + w);
   return ENIGMA_OK;
 }
 
@@ -211,8 +241,9 @@ int32_t enigma_check_timeout_path(int64_t polls, void* stream) {
   if (polls < 0 || polls > (int64_t(1) << 24)) return badarg("polls must be in [0, 2^24]");
   uint32_t* st = enigma::device_status();
   if (st == nullptr) return cuda_status(cudaErrorNoDevice, "device status");
-  timeout_probe_kernel<<<1, 32, 0, as_stream(stream)>>>(st, static_cast<long long>(polls));
-  return cuda_status(cudaGetLastError(), "timeout probe");
+  return cuda_status(enigma::launch_timeout_probe(st, static_cast<long long>(polls),
+                                                  as_stream(stream)),
+                     "timeout probe");
 }
 
 int32_t enigma_synchronize(void* stream) {

@@ -133,6 +133,7 @@ cudaError_t sdpa_simt_bf16_launch(const void* Q, const void* K, const void* V, v
 cudaError_t sdpa_f32_launch(const void* Q, const void* K, const void* V, void* O, int64_t B,
                             int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
                             float scale, bool causal, cudaStream_t s) {
+  note_kernel("sdpa_simt_kernel");
   return launch<float>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, D, scale, causal, s,
                        dense_strides(Hq, Hkv, Sq, Skv, D));
 }

@@ -27,8 +27,12 @@
 //               fp32 of those bf16 values, P stored with tcgen05.st over the first
 //               half of S's columns.  The softmax is issue-bound, so instructions per
 //               score are what counts.  O is rescaled only when a row max grows by
-//               more than 2^8 (exact: the numerator and denominator share the stale
-//               max).
+//               more than a factor 2 (exact: the numerator and denominator share the
+//               stale max).  The bound matters for accuracy: the exponent argument is
+//               rounded to bf16, whose error grows with |argument|, and with a stale
+//               max the largest keys of a row have positive arguments up to the bound.
+//               At 2^1 the largest weights see arguments in [-1, 1] (error <= 2^-9
+//               in log2 units); at 2^8 a peaked softmax (Q scaled x8) lost 2e-2.
 // All mbarrier waits are bounded (sm100.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -54,7 +58,7 @@ constexpr int LAUNCH_REGS = 168;
 constexpr int WG0_REGS = 104;
 constexpr int SOFTMAX_REGS = 200;
 static_assert(128 * WG0_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split");
-constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr float kRescaleThreshold = 1.0f;  // log2 units (see the header)
 
 template <int D>
 struct Cfg {
@@ -477,6 +481,7 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.status = enigma::device_status();
+  if (p.status == nullptr) return cudaErrorMemoryAllocation;   // the bounded waits need it
   dim3 grid(unsigned(int64_t(p.num_ctas_q) * B * Hq));
   sdpa_fwd_tc_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, s>>>(mq, mk, mv, p);
   return cudaGetLastError();

@@ -39,6 +39,7 @@ PROTOTYPES = {
     "enigma_stream_destroy": [_vp],
     "enigma_synchronize": [_vp],
     "enigma_last_error": [_c.c_char_p, _sz],
+    "enigma_last_kernel": [_c.c_char_p, _sz],
     "enigma_device_name": [_i32, _c.c_char_p, _sz],
     "enigma_device_attrs": [_i32, _c.POINTER(_i64), _c.POINTER(_i64), _c.POINTER(_i64),
                             _c.POINTER(_i64), _c.POINTER(_i32), _c.POINTER(_i32)],
@@ -65,6 +66,7 @@ PROTOTYPES = {
     "enigma_decode_layer_bf16": [_vp, _vp, _vp, _vp, _sz, _vp],
     "enigma_qwen_decode_f32": [_vp, _vp],
     "enigma_decode_layer_bf16_noalloc": [_vp, _vp, _vp, _vp],
+    "enigma_decode_noalloc_check_timeout_path": [_i64, _vp],
     "enigma_dispatch": [_i32, _c.POINTER(_vp), _i32, _c.POINTER(_i64), _i32, _c.POINTER(_f32),
                         _i32, _u32p, _u32p, _vp],
     "enigma_dispatch_timed": [_i32, _c.POINTER(_vp), _i32, _c.POINTER(_i64), _i32,
@@ -118,6 +120,13 @@ def last_error() -> str:
     buf = ctypes.create_string_buffer(512)
     lib().enigma_last_error(buf, 512)
     return buf.value.decode(errors="replace")
+
+
+def last_kernel() -> str:
+    """The device kernel the last operator call on this thread launched."""
+    buf = ctypes.create_string_buffer(128)
+    lib().enigma_last_kernel(buf, 128)
+    return buf.value.decode()
 
 
 def check(status: int, func: str) -> None:

@@ -19,8 +19,11 @@ Fingerprints (op kinds present in the trace, buffer signature):
              running-max buffer; 4 buffers (Q, KV, M0, O)
              -- examples/benchmark_sdpa.py:48-158
   sdpa_rows  exp + fmax + dot inside a carried loop (one query row per
-             thread); 4 buffers (Q, K, V, O)
-             -- examples/showcase_attention.py:31-125
+             thread); 4 buffers (Q, K, V, O); head_dim = the number of Q
+             elements a thread loads; (batch, head) slices along the grid's
+             y / z extent; causal when a score is replaced by a large negative
+             constant where the key index (loop-dependent) exceeds the query
+             row -- examples/showcase_attention.py:31-125
   gemm       dot of two 4-vectors into C (C = A B, or C += A B when C is
              also read) -- tests/metal/test_gemm_matmul_runtime.py:20-60;
              or async 2-D tile copies of A and B into threadgroup memory
@@ -114,6 +117,27 @@ class _Trace:
         return [op.attrs.get("value") for op in self.ops
                 if op.op == "const" and op.result.dtype.startswith(dtype_prefix)]
 
+    def depends_on_loop(self, v, _memo=None) -> bool:
+        """True when `v` is computed from the induction variable of a traced loop."""
+        if _memo is None:
+            _memo = {}
+            ivs = {id(op.attrs["iv"]) for op in self.ops if op.op == "scf_for" and "iv" in op.attrs}
+            _memo["ivs"] = ivs
+        if not isinstance(v, IRValue):
+            return False
+        if id(v) in _memo["ivs"]:
+            return True
+        if id(v) in _memo:
+            return _memo[id(v)]
+        _memo[id(v)] = False
+        op = self.producer.get(id(v))
+        r = op is not None and any(self.depends_on_loop(o, _memo) for o in op.operands)
+        _memo[id(v)] = r
+        return r
+
+    def loads_of(self, buffer: str) -> int:
+        return sum(1 for op in self.ops if op.op == "load" and op.attrs.get("buffer") == buffer)
+
     def vec_widths(self) -> List[int]:
         return [int(op.result.dtype[-1]) for op in self.ops if op.op == "make_vec"]
 
@@ -174,6 +198,33 @@ def _first_tensor(args, rank: int) -> Optional[Tensor]:
 
 
 # ----------------------------------------------------------------------------- sdpa
+_MASK_GT = {"cmp_gt": False, "cmp_ugt": False, "cmp_lt": True, "cmp_ult": True}
+
+
+def _causal_mask(t: _Trace) -> bool:
+    """Find `where(score, -big, key > row)`: a select whose taken value is a constant at or
+    below -1e20 under a strict comparison with the loop-dependent (key) side greater.
+    Returns False without such a select; raises for a mask of another shape, which no
+    sm_100a kernel here implements (e.g. key >= row, or a mask not tied to the key loop)."""
+    for op in t.ops:
+        if op.op != "select":
+            continue
+        _false, taken, cond = op.operands
+        c = t.const_of(taken)
+        if c is None or c > -1e20:
+            continue
+        cop = t.def_of(cond)
+        if cop is None or cop.op not in _MASK_GT:
+            raise EnigmaError("attention mask: only `key > query` (causal) masks are supported")
+        hi, lo = cop.operands
+        if _MASK_GT[cop.op]:
+            hi, lo = lo, hi
+        if t.depends_on_loop(hi) and not t.depends_on_loop(lo):
+            return True
+        raise EnigmaError("attention mask: only `key > query` (causal) masks are supported")
+    return False
+
+
 def _match_sdpa(t: _Trace, args: tuple) -> Optional[Binding]:
     if t.n_buffers() != 4 or not t.has("exp", "fmax"):
         return None
@@ -186,7 +237,7 @@ def _match_sdpa(t: _Trace, args: tuple) -> Optional[Binding]:
         return Binding("sdpa", dtype, {"scale": 1.0, "causal": False}, layout="gqa_interleaved")
     if t.has("dot") and t.kinds["scf_for"] >= 1:
         widths = t.vec_widths()
-        d = widths[0] if widths else None
+        d = t.loads_of(t.b.args[0][0]) or (widths[0] if widths else None)
         scale = None
         for op in t.ops:
             if op.op == "rsqrt":
@@ -199,7 +250,7 @@ def _match_sdpa(t: _Trace, args: tuple) -> Optional[Binding]:
                     src = t.source_of(o)
                     if isinstance(src, dict):
                         scale = src
-        params = {"scale": scale if scale is not None else 1.0, "causal": False}
+        params = {"scale": scale if scale is not None else 1.0, "causal": _causal_mask(t)}
         if d:
             params["head_dim"] = d
         q = _first_tensor(args, 2)

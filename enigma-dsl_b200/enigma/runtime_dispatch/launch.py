@@ -162,16 +162,24 @@ def _plan_sdpa(b, nbytes, grid, threads):
                          stream)
         return LaunchPlan(f"sdpa gqa tokens={tokens} Hq={hq} Hkv={hkv} D={d} "
                           f"kv_tokens={kv_tokens}", fn, (3,))
+    # One query row per thread along x; the grid's y * z extent counts the (batch, head)
+    # slices of dense [B*H, S, D] buffers (1 for the single-head showcase kernel).
     d = int(b.params["head_dim"])
-    sq = _div(nbytes[0], es * d, "attention Q")
-    sk = _div(nbytes[1], es * d, "attention K")
-    _need(nbytes[2] >= sk * d * es and nbytes[3] >= sq * d * es, "attention V / O too small")
+    bh = max(1, int(grid[1]) if len(grid) > 1 else 1) * max(1, int(grid[2]) if len(grid) > 2
+                                                            else 1)
+    sq = _div(nbytes[0], es * d * bh, "attention Q")
+    sk = _div(nbytes[1], es * d * bh, "attention K")
+    _need(nbytes[2] >= bh * sk * d * es and nbytes[3] >= bh * sq * d * es,
+          "attention V / O too small")
+    _need(int(grid[0]) <= sq or bh == 1,
+          f"grid.x = {grid[0]} query rows exceeds the {sq} rows of each (batch, head) slice")
     name = "enigma_sdpa_bf16" if b.dtype == "bfloat" else "enigma_sdpa_f32"
 
     def fn(p, stream):
-        _native.call(name, p[0], p[1], p[2], p[3], 1, 1, 1, sq, sk, d, ctypes.c_float(scale),
+        _native.call(name, p[0], p[1], p[2], p[3], 1, bh, bh, sq, sk, d, ctypes.c_float(scale),
                      causal, stream)
-    return LaunchPlan(f"sdpa rows Sq={sq} Sk={sk} D={d} scale={scale}", fn, (3,))
+    return LaunchPlan(f"sdpa rows heads={bh} Sq={sq} Sk={sk} D={d} scale={scale} "
+                      f"causal={bool(causal)}", fn, (3,))
 
 
 def _plan_elementwise(b, nbytes):

@@ -191,9 +191,13 @@ class MetalRuntime:
                 f"{hint}Outputs are appended AFTER inputs in the bind list. Pass every kernel "
                 f"parameter exactly once across inputs= / scalars= / output_size(s)/_shapes.")
 
-    def _bind(self, merged_inputs, out_sizes):
+    def _bind(self, merged_inputs, out_sizes, out_tensors=None):
+        """Device buffers in bind order.  CUDA tensors (inputs, and outputs when given) are
+        borrowed; the runtime's stream first waits for the work torch has queued on them
+        (the stream is non-blocking, so it would not otherwise order after torch's)."""
         torch = _torch_mod()
         bufs = _DeviceBuffers(self._stream)
+        borrowed = False
         try:
             for x in merged_inputs:
                 if torch is not None and isinstance(x, torch.Tensor):
@@ -203,13 +207,23 @@ class MetalRuntime:
                         bufs.add_host(x)
                     else:
                         bufs.add_tensor(x)
+                        borrowed = True
                 else:
                     bufs.add_host(x)
-            for sz in out_sizes:
-                bufs.add_empty(sz)
+            if out_tensors is not None:
+                for t in out_tensors:
+                    bufs.add_tensor(t)
+                borrowed = True
+            else:
+                for sz in out_sizes:
+                    bufs.add_empty(sz)
         except Exception:
             bufs.free()
             raise
+        if borrowed:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            torch.cuda.ExternalStream(self._stream, device=self.device).wait_event(ev)
         return bufs
 
     # ------------------------------------------------------------------ execute
@@ -242,7 +256,12 @@ class MetalRuntime:
         values = {"scalars": {sp[1]: v for sp, v in zip(scalar_params, scalars or [])},
                   "constants": {int(k): (v[1] if isinstance(v, tuple) else v)
                                 for k, v in (constants or {}).items()}}
-        bufs = self._bind(merged, out_sizes)
+        out_tensors = None
+        if torch_out:
+            # Outputs are torch tensors on this device: the kernels write them in place.
+            out_tensors = [torch.zeros(shp, dtype=dt, device=f"cuda:{self.device}")
+                           for shp, dt in zip(output_shapes, output_dtypes)]
+        bufs = self._bind(merged, out_sizes, out_tensors)
         try:
             keep = [i for i in range(len(bufs.ptrs)) if i not in scalar_slots]
             p = _launch.plan(binding, [bufs.nbytes[i] for i in keep], tuple(grid), tuple(threads),
@@ -255,15 +274,7 @@ class MetalRuntime:
                                  threads=threads, plan=p.describe, return_code=e.status) from e
             first_out = len(merged)
             if torch_out:
-                torch = _torch_mod()
-                res = []
-                for k, (shp, dt) in enumerate(zip(output_shapes, output_dtypes)):
-                    t = torch.empty(shp, dtype=dt, device=f"cuda:{self.device}")
-                    src = torch.frombuffer(bytearray(bufs.read(first_out + k, out_sizes[k])),
-                                           dtype=dt).reshape(shp)
-                    t.copy_(src)
-                    res.append(t)
-                return res if multi else res[0]
+                return out_tensors if multi else out_tensors[0]
             outs = [bufs.read(first_out + k, sz) for k, sz in enumerate(out_sizes)]
             return outs if multi else outs[0]
         finally:

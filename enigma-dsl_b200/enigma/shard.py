@@ -100,3 +100,35 @@ def sdpa_heads(q, k, v, scale: Optional[float] = None, causal: bool = False,
     if not gather:
         return o
     return gather_rows(o, units, group).reshape(B, Hq, S, D)
+
+
+def decode_shard_config(cfg, group=None):
+    """This rank's share of a decode batch: the same layer with `batch` = its sequences
+    (shard_range over cfg.batch).  Each rank builds its DecodeLayer from this config and
+    so holds only its sequences' KV cache; the weights are replicated."""
+    import dataclasses
+    world, rank = world_rank(group)
+    lo, hi = shard_range(cfg.batch, world, rank)
+    return dataclasses.replace(cfg, batch=hi - lo)
+
+
+def decode_sequences(layer, x, gather: bool = False, group=None, total_batch=None):
+    """One decode step of this rank's sequences.  `layer` was built from
+    decode_shard_config; x is either the whole batch [total_batch, hidden] (the rank's
+    rows are sliced) or this rank's rows [batch_local, hidden] (then gather=True needs
+    total_batch).  With gather=True every rank returns the whole batch's output."""
+    world, rank = world_rank(group)
+    n_local = layer.cfg.batch
+    if total_batch is None and (x.shape[0] != n_local or world == 1):
+        total_batch = x.shape[0]
+    if x.shape[0] != n_local:
+        lo, hi = shard_range(x.shape[0], world, rank)
+        if hi - lo != n_local:
+            raise ValueError(f"rank {rank}: layer holds {n_local} sequences, x gives {hi - lo}")
+        x = x[lo:hi].contiguous()
+    out = layer.step(x)
+    if not gather:
+        return out
+    if total_batch is None:
+        raise ValueError("gather=True with this rank's rows only needs total_batch")
+    return gather_rows(out, total_batch, group)

@@ -54,6 +54,12 @@ int32_t enigma_stream_create(void** stream);
 int32_t enigma_stream_destroy(void* stream);
 int32_t enigma_synchronize(void* stream);
 int32_t enigma_last_error(char* buf, size_t len);
+/* Name of the device kernel the last operator call on this thread chose (e.g.
+ * "gemm_bf16_pair_kernel", "sdpa_fwd_tc_kernel"); "" before any call.  No
+ * counterpart in the reference, whose Swift runtime runs one named pipeline per
+ * dispatch (libenigma_runtime.swift:132-214): here one operator picks between
+ * tensor-core and CUDA-core kernels by shape and alignment. */
+int32_t enigma_last_kernel(char* buf, size_t len);
 
 /* ---- capability queries: replace enigma_device_name,
  *      enigma_device_max_threadgroup_memory,
@@ -195,17 +201,26 @@ int32_t enigma_qwen_decode_f32(const enigma_qwen_decode_f32_desc* desc, void* st
  * Metal runtime always allocates buffers per call.)  The workspace is a fixed 16 MiB
  * device array inside this library, held on every GPU that loads it until the process
  * exits; a step that needs more (enigma_decode_workspace_bytes) is rejected with
- * ENIGMA_ERR_BADARG.  This call itself allocates nothing.  Its first call on a device
- * looks up the array's device address once (cudaGetSymbolAddress), so make that first
- * call before any stream capture.  All calls share the array: calls that overlap on the
- * GPU race, so serialize them on one stream. */
+ * ENIGMA_ERR_BADARG.  Its first call on a device looks up the array's device address once
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.  With lazy
+ * module loading (CUDA's default) that first call is also when the driver loads this
+ * library's device code on the device and commits the 16 MiB: it can fail for lack of
+ * device memory, so make it during set-up.  Later calls allocate nothing.  A bounded wait
+ * that runs out flags this entry's own static status word; enigma_synchronize and
+ * enigma_take_device_status report it (ENIGMA_ERR_TIMEOUT) once and clear it.  All calls
+ * share the array: calls that overlap on the GPU race, so serialize them on one stream. */
 int32_t enigma_decode_layer_bf16_noalloc(const enigma_decode_layer_desc* desc, const void* x,
                                          void* out, void* stream);
+/* Self-test of that reporting: the probe of enigma_check_timeout_path aimed at the
+ * no-allocation entry's status word. */
+int32_t enigma_decode_noalloc_check_timeout_path(int64_t polls, void* stream);
 
 /* ---- generic dispatch by kernel id: replaces enigma_dispatch /
  *      enigma_dispatch_timed (libenigma_runtime.swift:132-214).
  *      grid / threads are Metal-style totals (threads per axis, not groups),
- *      accepted for interface parity; the kernels pick their own CTA shapes.
+ *      accepted for interface parity and checked (no zero extent, at most 1024
+ *      threads per threadgroup; NULL = not given); the kernels pick their own
+ *      CTA shapes.
  *      dispatch_timed returns the device time of the launch in microseconds,
  *      measured with CUDA events on `stream`, and synchronizes. ---- */
 int32_t enigma_dispatch(int32_t kernel_id, void* const* buffers, int32_t n_buffers,
@@ -223,7 +238,8 @@ int32_t enigma_event_destroy(void* ev);
 int32_t enigma_event_record(void* ev, void* stream);
 int32_t enigma_event_elapsed_ms(void* start, void* stop, float* ms);
 
-/* Number of device-side timeouts flagged since the last call (and reset). */
+/* Number of device-side timeouts flagged since the last call (and reset): the library's
+ * per-device status word plus the no-allocation decode entry's word.  Allocates nothing. */
 int32_t enigma_take_device_status(int32_t* timeouts);
 /* Self-test of the timeout reporting: enqueues one CTA that waits on a barrier nothing
  * arrives on, gives up after `polls` polls (<= 2^24; microseconds) and flags the device status

@@ -35,11 +35,18 @@ import numpy as np
 def bf16_round(x: np.ndarray) -> np.ndarray:
     """Round fp32 to the nearest bf16 (ties to even), returned as fp32."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    lsb = (u >> 16) & 1
-    r = ((u + 0x7FFF + lsb) >> 16) << 16
-    out = r.astype(np.uint32).view(np.float32)
-    return np.where(np.isnan(x), x, out).astype(np.float32)
+    u = x.view(np.uint32)
+    # uint32 arithmetic: for every non-NaN pattern u + 0x8000 < 2^32, so nothing wraps;
+    # NaNs are passed through below.
+    r = (u >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
+    out = r.view(np.float32)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = x[nan]
+    return out
 
 
 def to_bf16_bits(x: np.ndarray) -> np.ndarray:

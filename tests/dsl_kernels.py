@@ -165,6 +165,122 @@ def make_fa(n_keys, bc=16):
     return fa_naive
 
 
+# ---------------------------------------------------------------- FlashAttention, any D
+# The showcase body (examples/showcase_attention.py:31-91) generalised the way a caller
+# writes it for config 4: D/4 float4 chunks per dot, (m, l, o[0..D-1]) carried, one
+# query row per thread; threadgroups along y pick the (batch, head) slice of a dense
+# [B*H, S, D] buffer.  causal=True masks key > query with where(s, -1e30, key > row).
+def _fa_any_body(Q, K, V, O, row, bh, seq_q, seq_k, D, bc, causal, out_dtype):
+    def u(v):
+        return enigma.metal_cast(v, "uint")
+
+    def f(x):
+        return enigma.metal_cast(x, "float")
+
+    qb = bh * u(seq_q * D) + row * u(D)
+    kvb = bh * u(seq_k * D)
+    qv = [enigma.make_float4(*[f(Q[qb + u(4 * c + i)]) for i in range(4)])
+          for c in range(D // 4)]
+    sc = enigma.rsqrt(enigma.metal_cast(D, "float"))
+    neg = enigma.metal_cast(-1e30, "float")
+    z = enigma.metal_cast(0, "float")
+    with enigma.for_range(0, enigma.metal_cast(seq_k // bc, "int"),
+                          init=[neg, z] + [z] * D) as (t, c):
+        tb = kvb + enigma.metal_cast(t, "uint") * u(bc * D)
+        s = []
+        for j in range(bc):
+            kb = tb + u(j * D)
+            acc = None
+            for cc in range(D // 4):
+                kv = enigma.make_float4(*[f(K[kb + u(4 * cc + i)]) for i in range(4)])
+                d = enigma.dot(qv[cc], kv)
+                acc = d if acc is None else acc + d
+            x = acc * sc
+            if causal:
+                key = enigma.metal_cast(t, "uint") * u(bc) + u(j)
+                x = enigma.where(x, neg, enigma.cmp_ugt(key, row))
+            s.append(x)
+        mt = s[0]
+        for x in s[1:]:
+            mt = enigma.fmax(mt, x)
+        mn = enigma.fmax(c[0], mt)
+        a = enigma.exp(c[0] - mn)
+        ps = [enigma.exp(x - mn) for x in s]
+        tot = ps[0]
+        for p in ps[1:]:
+            tot = tot + p
+        o = [a * c[2 + i] for i in range(D)]
+        for j in range(bc):
+            vb = tb + u(j * D)
+            o = [enigma.fma(ps[j], f(V[vb + u(i)]), o[i]) for i in range(D)]
+        c[1] = a * c[1] + tot
+        c[0] = mn
+        for i in range(D):
+            c[2 + i] = o[i]
+    inv = enigma.metal_cast(1, "float") / c[1]
+    for i in range(D):
+        O[qb + u(i)] = enigma.metal_cast(c[2 + i] * inv, out_dtype)
+
+
+def make_fa_heads(seq, D, causal, bc=16, dtype="bfloat"):
+    """@enigma.kernel form: dispatch with grid=(seq, B*H, 1), threads=(BR, 1, 1)."""
+    ann = enigma.bf16 if dtype == "bfloat" else enigma.f32
+
+    def body(Q, K, V, O):
+        row = enigma.thread_position_in_grid_xyz("x")
+        bh = enigma.threadgroup_position_in_grid("y")
+        _fa_any_body(Q, K, V, O, row, bh, seq, seq, D, bc, causal, dtype)
+
+    if causal:
+        @enigma.kernel
+        def fa_causal(Q: ann, K: ann, V: ann, O: ann):
+            body(Q, K, V, O)
+        return fa_causal
+
+    @enigma.kernel
+    def fa_heads(Q: ann, K: ann, V: ann, O: ann):
+        body(Q, K, V, O)
+    return fa_heads
+
+
+# ---------------------------------------------------------------- FlashAttention, TV launcher
+# examples/showcase_attention.py:94-131: the same body launched from a TV layout,
+# thread layout (BR, 1) x value layout (1, D), grid from zipped_divide of Q by the tiler.
+# With heads > 1 the launcher adds a y extent of B*H over per-head (S, D) tensors.
+def make_fa_tv(M, N, D, BR=32, bc=16, heads=1, causal=False, dtype="float"):
+    from enigma._tracing import Tensor as TTensor
+
+    @enigma.kernel
+    def fa_tv_kernel(Q, K, V, O):
+        Qt = TTensor(Q.name, Q.buffer_index, Q.metal_dtype)
+        Kt = TTensor(K.name, K.buffer_index, K.metal_dtype)
+        Vt = TTensor(V.name, V.buffer_index, V.metal_dtype)
+        Ot = TTensor(O.name, O.buffer_index, O.metal_dtype)
+        tidx, _, _ = enigma.arch.thread_idx()
+        bidx, _, _ = enigma.arch.block_idx()
+        bdim, _, _ = enigma.arch.block_dim()
+        row = bidx * bdim + tidx
+        bh = enigma.threadgroup_position_in_grid("y") if heads > 1 else 0
+        _fa_any_body(Qt, Kt, Vt, Ot, row, bh, M, N, D, bc, causal, dtype)
+
+    @enigma.jit
+    def fa_tv(mQ, mK, mV, mO):
+        thr_layout = enigma.make_ordered_layout((BR, 1), order=(1, 0))
+        val_layout = enigma.make_ordered_layout((1, D), order=(1, 0))
+        tiler_mn, tv_layout = enigma.make_layout_tv(thr_layout, val_layout)
+        gQ = tensor_zipped_divide(mQ, tiler_mn)
+        num_blocks = enigma.size(gQ, mode=[1])
+        threads = enigma.size(tv_layout, mode=[0])
+        fa_tv_kernel(mQ, mK, mV, mO).launch(grid=(num_blocks * threads, heads, 1),
+                                            block=(threads, 1, 1))
+
+    args = (Tensor("Q", 0, dtype, enigma.Layout((M, D), (D, 1))),
+            Tensor("K", 1, dtype, enigma.Layout((N, D), (D, 1))),
+            Tensor("V", 2, dtype, enigma.Layout((N, D), (D, 1))),
+            Tensor("O", 3, dtype, enigma.Layout((M, D), (D, 1))))
+    return fa_tv, args
+
+
 # ---------------------------------------------------------------- K = 4 matmul / gemm
 # tests/metal/test_gemm_matmul_runtime.py:20-60
 def make_k4(n_cols, accumulate):
@@ -193,15 +309,17 @@ def make_k4(n_cols, accumulate):
 # ---------------------------------------------------------------- async-copy tiled GEMM
 # examples/async_copy_gemm.py:32-79: A/B tiles staged into threadgroup memory with 2-D
 # async copies, K loop over tiles.
-def make_async_gemm(m, n, k, tm=32, tn=32, tk=16):
+def make_async_gemm(m, n, k, tm=32, tn=32, tk=16, dtype="float"):
+    ann = enigma.bf16 if dtype == "bfloat" else enigma.f32
+
     @enigma.kernel
-    def gemm_async(A: enigma.f32, B: enigma.f32, C: enigma.f32):
+    def gemm_async(A: ann, B: ann, C: ann):
         tg = enigma.threadgroup_position_in_grid()
         cols = enigma.metal_cast(n // tn, "uint")
         bx, by = tg / cols, tg % cols
         sg = enigma.simdgroup_index_in_threadgroup()
-        a_tile = enigma.threadgroup_alloc("float", tm * tk)
-        b_tile = enigma.threadgroup_alloc("float", tk * tn)
+        a_tile = enigma.threadgroup_alloc(dtype, tm * tk)
+        b_tile = enigma.threadgroup_alloc(dtype, tk * tn)
         acc = enigma.register_tensor((2, 2), dtype="float", fill=0.0)
         zero = enigma.metal_cast(0, "uint")
         kc = enigma.metal_cast(k, "uint")

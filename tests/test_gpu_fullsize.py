@@ -2,7 +2,7 @@
 result would take minutes): RMSNorm bf16 262144 x 8192 (64 rows), GEMM bf16 8192^3 (64 full
 rows of C), SDPA bf16 [8, 32, 8192, 128] causal and non-causal (8 (b, h) pairs x 16 query
 rows).  Inputs are generated on the GPU from a seeded generator; only the sampled slices
-come back to the host.  Tolerances: BASELINE's max-abs <= 2e-2 and relative Frobenius
+come back to the host.  SDPA runs at S = 1024 and 4096 as well (config 4's other lengths).  Tolerances: BASELINE's max-abs <= 2e-2 and relative Frobenius
 <= 5e-3 for bf16 GEMM / SDPA, one bf16 ulp of the fp64 result for RMSNorm."""
 import numpy as np
 import pytest
@@ -48,14 +48,17 @@ def test_gemm_bf16_8192(cuda):
     del a, b, c
 
 
+@pytest.mark.parametrize("S", [1024, 4096, 8192])
 @pytest.mark.parametrize("causal", [True, False])
-def test_sdpa_bf16_8x32x8192x128(cuda, causal):
+def test_sdpa_bf16_8x32xSx128(cuda, causal, S):
+    """Config 4 at every listed sequence length, causal and non-causal."""
     import torch
-    from enigma import cuda_ops
-    B, H, S, D = 8, 32, 8192, 128
+    from enigma import cuda_ops, _native
+    B, H, D = 8, 32, 128
     g = torch.Generator(device=cuda).manual_seed(1)
     q, k, v = (torch.randn(B, H, S, D, device=cuda, generator=g).bfloat16() for _ in range(3))
     o = cuda_ops.sdpa(q, k, v, scale=1.0 / D ** 0.5, causal=causal)
+    assert _native.last_kernel() == "sdpa_fwd_tc_kernel"
     rng = np.random.default_rng(5)
     pairs = [(int(rng.integers(B)), int(rng.integers(H))) for _ in range(8)]
     rows = np.sort(np.concatenate([[0, S - 1], rng.integers(0, S, 14)]))

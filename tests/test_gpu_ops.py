@@ -135,6 +135,27 @@ def test_sdpa_bf16(cuda, b, hq, hk, sq, sk, d, causal):
     _check_bf16(_np(o), orc.sdpa(q, k, v, scale, causal))
 
 
+@pytest.mark.parametrize("q_scale", [4.0, 8.0])
+@pytest.mark.parametrize("causal", [False, True])
+def test_sdpa_bf16_peaked(cuda, q_scale, causal):
+    """A peaked softmax: Q scaled x4 / x8 puts scores at tens of units, so a few keys
+    carry each row and the exponent arguments span a wide range (the kernel's exponent
+    path is exercised far from the unit-variance case)."""
+    import torch
+    from enigma import cuda_ops, _native
+    rng = np.random.default_rng(11)
+    b, h, s, d = 2, 4, 1024, 128
+    q = orc.bf16_round(q_scale * rng.standard_normal((b, h, s, d), dtype=np.float32))
+    k = orc.bf16_round(rng.standard_normal((b, h, s, d), dtype=np.float32))
+    v = orc.bf16_round(rng.standard_normal((b, h, s, d), dtype=np.float32))
+    scale = 1.0 / np.sqrt(d)
+    o = cuda_ops.sdpa(_t(q, torch.bfloat16, cuda), _t(k, torch.bfloat16, cuda),
+                      _t(v, torch.bfloat16, cuda), scale=scale, causal=causal)
+    torch.cuda.synchronize()
+    assert _native.last_kernel() == "sdpa_fwd_tc_kernel"
+    _check_bf16(_np(o), orc.sdpa(q, k, v, scale, causal))
+
+
 def test_sdpa_f32_fa_d4(cuda):
     """FlashAttention showcase shape: M = N = 1024, D = 4, scale 1/sqrt(D)
     (examples/showcase_attention.py:22-26, check at :150-153)."""

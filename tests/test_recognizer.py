@@ -107,3 +107,49 @@ def test_runtime_eps_resolution():
                     {"scalars": {}, "constants": {}})
     with pytest.raises(RuntimeError, match="execute"):
         launch.plan(b, [8 * 1024 * 4, 1024 * 4, 8 * 1024 * 4], (1, 1, 1), (1, 1, 1))
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_fa_heads_binding_d128(causal):
+    b = enigma.compile(K.make_fa_heads(1024, 128, causal)).cuda_kernel
+    assert (b.op, b.dtype, b.layout, b.params["head_dim"], b.params["causal"]) == \
+        ("sdpa", "bfloat", "rows", 128, causal)
+    assert b.params["scale"] == pytest.approx(128 ** -0.5)
+
+
+def test_fa_tv_binding_reference_shape():
+    """fa_tv (showcase_attention.py:104-131): grid from zipped_divide(Q, (32, 4))."""
+    jit, args = K.make_fa_tv(1024, 1024, 4)
+    ck = enigma.compile(jit, *args)
+    b = ck.cuda_kernel
+    assert (b.op, b.layout, b.params["head_dim"], b.params["seq_q"], b.params["causal"]) == \
+        ("sdpa", "rows", 4, 1024, False)
+    assert ck.grid == (1024, 1, 1) and ck.block == (32, 1, 1)
+
+
+def test_async_gemm_bf16_binding():
+    b = enigma.compile(K.make_async_gemm(4096, 4096, 4096, dtype="bfloat")).cuda_kernel
+    assert (b.op, b.dtype, b.params["K"], b.params["N"]) == ("gemm", "bfloat", 4096, 4096)
+
+
+def test_unsupported_mask_raises():
+    """A mask that keeps key > query (anti-causal) has no sm_100a kernel."""
+    @enigma.kernel
+    def fa_anti(Q: enigma.f32, K_: enigma.f32, V: enigma.f32, O: enigma.f32):
+        row = enigma.thread_position_in_grid
+        neg = enigma.metal_cast(-1e30, "float")
+        z = enigma.metal_cast(0, "float")
+        with enigma.for_range(0, 16, init=[neg, z, z]) as (t, c):
+            s = Q[row] * K_[t]
+            s = enigma.where(s, neg, enigma.cmp_ult(enigma.metal_cast(t, "uint"), row))
+            qv = enigma.make_float4(Q[row], Q[row], Q[row], Q[row])
+            s = s + enigma.dot(qv, qv)
+            mn = enigma.fmax(c[0], s)
+            p = enigma.exp(s - mn)
+            c[1] = c[1] * enigma.exp(c[0] - mn) + p
+            c[2] = c[2] + p * V[t]
+            c[0] = mn
+        O[row] = c[2] / c[1]
+
+    with pytest.raises(enigma.EnigmaError, match="key > query"):
+        enigma.compile(fa_anti)
