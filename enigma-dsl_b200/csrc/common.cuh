@@ -35,6 +35,9 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
                              int64_t K, cudaStream_t s);
 cudaError_t gemm_f32_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
                             int64_t K, bool accumulate, cudaStream_t s);
+cudaError_t gemm_f32_trans_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                  int64_t K, bool trans_a, bool trans_b, bool accumulate,
+                                  cudaStream_t s);
 cudaError_t sdpa_f32_launch(const void* Q, const void* K, const void* V, void* O, int64_t B,
                             int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
                             float scale, bool causal, cudaStream_t s);

@@ -411,15 +411,18 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
 template <typename T>
 __global__ void __launch_bounds__(256)
 gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B, T* __restrict__ C, int M,
-                 int N, int K, int accumulate) {
+                 int N, int K, int accumulate, int trans_a = 0, int trans_b = 0) {
   __shared__ float sa[16][17];
   __shared__ float sb[16][17];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int row = blockIdx.y * 16 + ty, col = blockIdx.x * 16 + tx;
   float acc = 0.f;
   for (int k0 = 0; k0 < K; k0 += 16) {
-    sa[ty][tx] = (row < M && k0 + tx < K) ? float(A[int64_t(row) * K + k0 + tx]) : 0.f;
-    sb[ty][tx] = (k0 + ty < K && col < N) ? float(B[int64_t(k0 + ty) * N + col]) : 0.f;
+    // A is [M, K] row-major, or [K, M] when trans_a; B is [K, N], or [N, K] when trans_b.
+    const int64_t ia = trans_a ? int64_t(k0 + tx) * M + row : int64_t(row) * K + k0 + tx;
+    const int64_t ib = trans_b ? int64_t(col) * K + k0 + ty : int64_t(k0 + ty) * N + col;
+    sa[ty][tx] = (row < M && k0 + tx < K) ? float(A[ia]) : 0.f;
+    sb[ty][tx] = (k0 + ty < K && col < N) ? float(B[ib]) : 0.f;
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < 16; ++k) acc = fmaf(sa[ty][k], sb[k][tx], acc);
@@ -516,6 +519,19 @@ cudaError_t gemm_f32_launch(const void* A, const void* B, void* C, int64_t M, in
                                                static_cast<const float*>(B),
                                                static_cast<float*>(C), int(M), int(N), int(K),
                                                accumulate ? 1 : 0);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_f32_trans_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                  int64_t K, bool trans_a, bool trans_b, bool accumulate,
+                                  cudaStream_t s) {
+  dim3 grid(unsigned((N + 15) / 16), unsigned((M + 15) / 16));
+  note_kernel("gemm_simt_kernel");
+  gemm_simt_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(A),
+                                               static_cast<const float*>(B),
+                                               static_cast<float*>(C), int(M), int(N), int(K),
+                                               accumulate ? 1 : 0, trans_a ? 1 : 0,
+                                               trans_b ? 1 : 0);
   return cudaGetLastError();
 }
 

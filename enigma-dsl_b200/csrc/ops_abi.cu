@@ -166,6 +166,21 @@ int32_t enigma_gemm_f32(const void* A, const void* B, void* C, int64_t M, int64_
                        "gemm_f32");
 }
 
+int32_t enigma_gemm_f32_trans(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                              int64_t K, int32_t trans_a, int32_t trans_b, int32_t accumulate,
+                              void* stream) {
+  if (M < 0 || N < 0 || K < 0) return bad("gemm: negative size");
+  if (M > (1ll << 31) - 1 || N > (1ll << 31) - 1 || K > (1ll << 31) - 1)
+    return bad("gemm: sizes must fit in int32");
+  if (M == 0 || N == 0) return ENIGMA_OK;
+  if (A == nullptr || B == nullptr || C == nullptr) return bad("gemm: NULL buffer");
+  if (!aligned(A, 4) || !aligned(B, 4) || !aligned(C, 4)) return bad("gemm: misaligned buffer");
+  return launch_status(enigma::gemm_f32_trans_launch(A, B, C, M, N, K, trans_a != 0,
+                                                     trans_b != 0, accumulate != 0,
+                                                     as_stream(stream)),
+                       "gemm_f32_trans");
+}
+
 int32_t enigma_sdpa_f32(const void* Q, const void* K, const void* V, void* O, int64_t batch,
                         int64_t heads_q, int64_t heads_kv, int64_t seq_q, int64_t seq_kv,
                         int64_t head_dim, float scale, int32_t causal, void* stream) {

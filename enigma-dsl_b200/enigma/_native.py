@@ -55,6 +55,7 @@ PROTOTYPES = {
     "enigma_sdpa_bf16": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp],
     "enigma_elementwise": [_i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "enigma_gemm_f32": [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp],
+    "enigma_gemm_f32_trans": [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp],
     "enigma_sdpa_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _vp],
     "enigma_sdpa_strided": [_i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                             _c.POINTER(_i64), _f32, _i32, _vp],

@@ -24,7 +24,8 @@ Fingerprints (op kinds present in the trace, buffer signature):
              y / z extent; causal when a score is replaced by a large negative
              constant where the key index (loop-dependent) exceeds the query
              row -- examples/showcase_attention.py:31-125
-  gemm       dot of two 4-vectors into C (C = A B, or C += A B when C is
+  gemm       one enigma.gemm tile op (fp32; shape and transposes from its marker)
+             -- enigma/ops/gemm.py:51-167; or dot of two 4-vectors into C (C = A B, or C += A B when C is
              also read) -- tests/metal/test_gemm_matmul_runtime.py:20-60;
              or async 2-D tile copies of A and B into threadgroup memory
              -- examples/async_copy_gemm.py:32-79 (bound to the GEMM it
@@ -266,6 +267,18 @@ def _match_gemm(t: _Trace, args: tuple) -> Optional[Binding]:
     if len(t.b.args) != 3:
         return None
     dtype = t.b.args[0][2]
+    tiles = [op for op in t.ops if op.op == "tile_gemm"]
+    if tiles:
+        # One enigma.gemm tile op over tiles staged from A and B (enigma/ops/gemm.py:51-167;
+        # tests/metal/test_new_features_runtime.py:25-56): Out = A @ B for the whole tile.
+        if len(tiles) != 1 or t.kinds["exp"]:
+            return None
+        a = tiles[0].attrs
+        if dtype != "float" or a["accum_dtype"] != "float":
+            raise EnigmaError("enigma.gemm tile op: only fp32 tiles have an sm_100a binding")
+        return Binding("gemm", dtype, {"M": a["M"], "N": a["N"], "K": a["K"],
+                                       "transpose_A": a["transpose_A"],
+                                       "transpose_B": a["transpose_B"]}, layout="tile")
     if t.has("async_copy_2d_d2t"):
         uints = [c for c in t.consts("uint") if isinstance(c, int)]
         # The example names K and the B/C row pitch with metal_cast(..., "uint").

@@ -12,7 +12,7 @@ from __future__ import annotations
 
 from typing import Optional
 
-from ._tracing import (EnigmaError, RegisterTensor, _ensure_ir, _require_builder, cmp_ge,
+from ._tracing import (EnigmaError, IROp, RegisterTensor, _ensure_ir, _require_builder, cmp_ge,
                        extract_bits, fma, insert_bits, make_filled_simdgroup_matrix, metal_cast,
                        select, simdgroup_matrix_load, simdgroup_matrix_store,
                        simdgroup_multiply_accumulate)
@@ -22,8 +22,12 @@ from .tensor import Tensor
 def gemm(A_s, B_s, C, *, M: int, N: int, K: int, transpose_A: bool = False,
          transpose_B: bool = False, accum_dtype: str = "float",
          use_simdgroup: Optional[bool] = None) -> None:
-    """Record C += A @ B over an M x N tile with reduction K."""
-    _require_builder("gemm")
+    """Record C += A @ B over an M x N tile with reduction K.
+
+    Besides the per-element ops, a `tile_gemm` marker op carries the tile's shape and
+    transpose flags: the recognizer binds a kernel built around one tile GEMM to the
+    fp32 GEMM kernel (enigma_gemm_f32_trans)."""
+    b = _require_builder("gemm")
     if M <= 0 or N <= 0 or K <= 0:
         raise EnigmaError(f"gemm: M/N/K must be positive, got M={M}, N={N}, K={K}")
     matrix_ok = (M, N, K) == (8, 8, 8) and accum_dtype in ("float", "half") \
@@ -32,6 +36,10 @@ def gemm(A_s, B_s, C, *, M: int, N: int, K: int, transpose_A: bool = False,
         raise EnigmaError(f"gemm: use_simdgroup=True but shape ({M}x{N}x{K}, elem={accum_dtype}) "
                           f"is not 8x8x8 (or transpose flags set). The simdgroup path currently "
                           f"supports a single 8x8x8 tile only.")
+    b.record(IROp("tile_gemm", None, [], {"M": int(M), "N": int(N), "K": int(K),
+                                          "transpose_A": bool(transpose_A),
+                                          "transpose_B": bool(transpose_B),
+                                          "accum_dtype": accum_dtype}))
     if matrix_ok if use_simdgroup is None else use_simdgroup:
         if not isinstance(C, Tensor):
             raise EnigmaError("gemm: simdgroup path requires C to be a Tensor (threadgroup or "

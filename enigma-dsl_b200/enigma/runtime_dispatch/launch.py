@@ -96,6 +96,15 @@ def _plan_rmsnorm(b, nbytes):
 def _plan_gemm(b, nbytes):
     _need(len(nbytes) == 3, f"gemm binds 3 buffers (A, B, C), got {len(nbytes)}")
     es = _ES[b.dtype]
+    if b.layout == "tile":
+        m, n, k = (int(b.params[x]) for x in "MNK")
+        ta, tb = int(bool(b.params["transpose_A"])), int(bool(b.params["transpose_B"]))
+        _need(nbytes[0] >= m * k * es and nbytes[1] >= k * n * es and nbytes[2] >= m * n * es,
+              f"gemm tile {m}x{n}x{k}: a buffer is smaller than its tile")
+
+        def fn(p, stream):
+            _native.call("enigma_gemm_f32_trans", p[0], p[1], p[2], m, n, k, ta, tb, 0, stream)
+        return LaunchPlan(f"gemm tile M={m} N={n} K={k} transA={ta} transB={tb}", fn, (2,))
     k = int(b.params["K"])
     m = _div(nbytes[0], es * k, "gemm A")
     n = int(b.params.get("N") or _div(nbytes[1], es * k, "gemm B"))

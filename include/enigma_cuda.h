@@ -116,6 +116,13 @@ int32_t enigma_elementwise(int32_t op, int32_t dtype, const void* A, const void*
  * (tests/metal/test_gemm_matmul_runtime.py:20-60); `accumulate` != 0 adds into C. */
 int32_t enigma_gemm_f32(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                         int32_t accumulate, void* stream);
+/* The same with either operand transposed: A is [K, M] when trans_a, B is [N, K] when
+ * trans_b — replaces the tile op enigma.gemm(A_s, B_s, C, M, N, K, transpose_A,
+ * transpose_B) (enigma/ops/gemm.py:51-167; C += A @ B, C starting from the zero-filled
+ * register tile, tests/metal/test_new_features_runtime.py:25-56). */
+int32_t enigma_gemm_f32_trans(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                              int64_t K, int32_t trans_a, int32_t trans_b, int32_t accumulate,
+                              void* stream);
 /* fp32 attention, same layout and masking as enigma_sdpa_bf16 (showcase_attention.py:31-125,
  * benchmark_sdpa.py:48-150 with the KV de-interleaved). */
 int32_t enigma_sdpa_f32(const void* Q, const void* K, const void* V, void* O, int64_t batch,

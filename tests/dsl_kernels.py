@@ -306,6 +306,29 @@ def make_k4(n_cols, accumulate):
     return matmul_k4
 
 
+# ---------------------------------------------------------------- enigma.gemm tile op
+# tests/metal/test_new_features_runtime.py:25-56: stage A and B into threadgroup tiles,
+# one enigma.gemm into a zero-filled register tile, store the tile.
+def make_tile_gemm(M, N, K, transpose_A=False, transpose_B=False):
+    @enigma.kernel
+    def tile_gemm(A: enigma.f32, B: enigma.f32, Out: enigma.f32):
+        A_s = enigma.threadgroup_alloc("float", M * K)
+        B_s = enigma.threadgroup_alloc("float", K * N)
+        for i in range(M * K):
+            A_s[i] = A[i]
+        for i in range(K * N):
+            B_s[i] = B[i]
+        enigma.barrier("mem_threadgroup")
+        C = enigma.register_tensor((M, N), dtype="float", fill=0.0)
+        enigma.gemm(A_s, B_s, C, M=M, N=N, K=K, transpose_A=transpose_A,
+                    transpose_B=transpose_B)
+        for m in range(M):
+            for n in range(N):
+                Out[m * N + n] = C[m, n]
+
+    return tile_gemm
+
+
 # ---------------------------------------------------------------- async-copy tiled GEMM
 # examples/async_copy_gemm.py:32-79: A/B tiles staged into threadgroup memory with 2-D
 # async copies, K loop over tiles.

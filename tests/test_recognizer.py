@@ -153,3 +153,11 @@ def test_unsupported_mask_raises():
 
     with pytest.raises(enigma.EnigmaError, match="key > query"):
         enigma.compile(fa_anti)
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True)])
+def test_tile_gemm_binding(ta, tb):
+    """enigma.gemm tile op (enigma/ops/gemm.py:51-167) at the reference test's 3x4x2."""
+    b = enigma.compile(K.make_tile_gemm(3, 4, 2, ta, tb)).cuda_kernel
+    assert (b.op, b.layout, b.params["M"], b.params["N"], b.params["K"]) == ("gemm", "tile", 3, 4, 2)
+    assert (b.params["transpose_A"], b.params["transpose_B"]) == (ta, tb)
