@@ -332,20 +332,20 @@ def test_dsl_fa_prepare_dispatch_timed(rt):
         prep.release()
 
 
-@pytest.mark.parametrize("M,N,K,ta,tb", [(3, 4, 2, False, False), (3, 4, 2, True, False),
+@pytest.mark.parametrize("M,N,Kd,ta,tb", [(3, 4, 2, False, False), (3, 4, 2, True, False),
                                          (5, 7, 6, False, True), (8, 8, 8, False, False)])
-def test_tile_gemm(rt, M, N, K, ta, tb):
+def test_tile_gemm(rt, M, N, Kd, ta, tb):
     """The reference's enigma.gemm runtime test (test_new_features_runtime.py:25-56: 3x4x2,
     grid (1,1,1), rtol 1e-5) and transposed / 8x8x8 tiles."""
     from enigma import _native
-    ck = enigma.compile(K.make_tile_gemm(M, N, K, ta, tb))
-    if (M, N, K) == (3, 4, 2) and not (ta or tb):
+    ck = enigma.compile(K.make_tile_gemm(M, N, Kd, ta, tb))
+    if (M, N, Kd) == (3, 4, 2) and not (ta or tb):
         a = np.array([[1, 2], [3, 4], [5, 6]], dtype=np.float32)
         b = np.array([[7, 8, 9, 10], [11, 12, 13, 14]], dtype=np.float32)
     else:
-        rng = np.random.default_rng(M * N * K)
-        a = rng.standard_normal((M, K)).astype(np.float32)
-        b = rng.standard_normal((K, N)).astype(np.float32)
+        rng = np.random.default_rng(M * N * Kd)
+        a = rng.standard_normal((M, Kd)).astype(np.float32)
+        b = rng.standard_normal((Kd, N)).astype(np.float32)
     a_buf = a.T.copy() if ta else a
     b_buf = b.T.copy() if tb else b
     raw = rt.execute(ck, [a_buf.ravel(), b_buf.ravel()], M * N * 4, grid=(1, 1, 1),
