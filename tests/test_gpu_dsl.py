@@ -333,7 +333,7 @@ def test_dsl_fa_prepare_dispatch_timed(rt):
 
 
 @pytest.mark.parametrize("M,N,Kd,ta,tb", [(3, 4, 2, False, False), (3, 4, 2, True, False),
-                                         (5, 7, 6, False, True), (8, 8, 8, False, False)])
+                                         (5, 7, 6, False, True), (8, 8, 6, False, False)])
 def test_tile_gemm(rt, M, N, Kd, ta, tb):
     """The reference's enigma.gemm runtime test (test_new_features_runtime.py:25-56: 3x4x2,
     grid (1,1,1), rtol 1e-5) and transposed / 8x8x8 tiles."""

@@ -120,7 +120,11 @@ def test_gemm_f32_k4(cuda, m):
     (2, 4, 2, 256, 256, 64, True), (1, 1, 1, 100, 77, 128, False), (1, 1, 1, 77, 100, 128, True),
     (1, 8, 1, 1, 300, 64, False), (1, 2, 1, 300, 200, 64, True), (1, 2, 2, 2048, 2048, 128, True),
     (1, 2, 2, 2048, 2048, 128, False), (2, 2, 1, 129, 1000, 64, False), (1, 1, 1, 1, 1, 128, True),
-    (1, 1, 1, 5, 3, 16, False)])
+    (1, 1, 1, 5, 3, 16, False),
+    # more items than SMs (the persistent loop walks several per CTA), including items
+    # whose second query tile lies entirely past Sq (Sq = 800), GQA, and Sq < Sk causal
+    (2, 64, 8, 800, 800, 128, True), (2, 64, 64, 800, 800, 64, False),
+    (1, 160, 160, 300, 1000, 128, True), (4, 48, 16, 1024, 1024, 128, True)])
 def test_sdpa_bf16(cuda, b, hq, hk, sq, sk, d, causal):
     import torch
     from enigma import cuda_ops
