@@ -43,13 +43,13 @@ sys.path.insert(0, str(ROOT / "enigma-dsl_b200"))
 ROWS, HIDDEN, EPS = 262144, 8192, 1e-6
 METRIC = "RMSNorm HBM GB/s (bf16 262144x8192, fp32 accumulate)"
 BYTES_PER_STEP = 4 * ROWS * HIDDEN + 2 * HIDDEN
-# DRAM bytes (read + write) per algorithmic byte of one rmsnorm launch, from an ncu
-# capture (dram__bytes_read.sum + dram__bytes_write.sum) of a 32768 x 8192 launch, scaled
-# to the launch timed here by its bytes.  Writes still held in L2 when the kernel ends are
-# not in the capture, so it reads slightly below 1.
-NCU_TRAFFIC_PER_BYTE = 8_192_407_552 / 8_589_950_976
-NCU_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of a 32768 x 8192 "
-                      "launch, scaled by bytes; excludes writes still in L2 at kernel end")
+# DRAM bytes (read + write) per algorithmic byte of one rmsnorm launch, from an ncu capture
+# (dram__bytes_read.sum 4.30 GB + dram__bytes_write.sum 4.25 GB, one pass) of the full
+# 262144 x 8192 launch; scaled by bytes for the smaller row shards of N > 1.  Writes still
+# held in L2 when the kernel ends are not in the capture, so it reads slightly below 1.
+NCU_TRAFFIC_PER_BYTE = 8.55e9 / 8_589_950_976
+NCU_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the full 262144 x "
+                      "8192 launch (3 significant digits), scaled by bytes for smaller shards")
 
 
 def _set_rows(rows: int) -> None:
