@@ -17,6 +17,11 @@ int sm_count();
 uint32_t* device_status();
 // The same word if it already exists on the current device, else nullptr (never allocates).
 uint32_t* device_status_if_exists();
+// A pair of work counters of the current device for one launch (a dynamic work queue:
+// [0] next item, [1] spare), taken round-robin from a per-device pool so launches in flight
+// on different streams use different pairs; the caller zeroes it on its stream before the
+// launch.  nullptr if the per-device state could not be created.
+uint32_t* work_counters();
 // Reads and clears the no-allocation decode entry's status word on the current device
 // (0 if that entry has not run there).  Allocates nothing.
 cudaError_t noalloc_take_status(uint32_t* value);

@@ -5,6 +5,7 @@
 // creation, buffers, dispatch by kernel, timed dispatch and capability queries.
 // Argument checks happen here, before anything is launched, and map to
 // ENIGMA_ERR_BADARG with a message for enigma_last_error.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -23,6 +24,11 @@ int g_sms[kMaxDev] = {0};
 uint32_t* g_status[kMaxDev] = {nullptr};
 cudaStream_t g_aux[kMaxDev] = {nullptr};
 
+// Per-device state: the status word (bytes 0..255) and kWorkSlots pairs of work counters.
+constexpr int kWorkSlots = 4096;
+constexpr size_t kStateBytes = 256 + size_t(kWorkSlots) * 2 * sizeof(uint32_t);
+std::atomic<uint32_t> g_work_next[kMaxDev];
+
 int current_device() {
   int d = 0;
   cudaGetDevice(&d);
@@ -38,9 +44,9 @@ cudaError_t ensure_device_state(int dev) {
   cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   uint32_t* st = nullptr;
-  e = cudaMalloc(&st, 256);
+  e = cudaMalloc(&st, kStateBytes);
   if (e != cudaSuccess) return e;
-  e = cudaMemset(st, 0, 256);
+  e = cudaMemset(st, 0, kStateBytes);
   if (e != cudaSuccess) return e;
   g_sms[dev] = sms;
   g_status[dev] = st;
@@ -69,6 +75,13 @@ uint32_t* device_status() {
   const int d = current_device();
   if (ensure_device_state(d) != cudaSuccess) return nullptr;
   return g_status[d];
+}
+
+uint32_t* work_counters() {
+  const int d = current_device();
+  if (ensure_device_state(d) != cudaSuccess) return nullptr;
+  const uint32_t slot = g_work_next[d].fetch_add(1, std::memory_order_relaxed) % kWorkSlots;
+  return g_status[d] + 64 + 2 * slot;
 }
 
 uint32_t* device_status_if_exists() {

@@ -66,7 +66,7 @@ struct Cfg {
   static constexpr int Q_BYTES = BM * D * 2;     // one Q tile
   static constexpr int KV_BYTES = BN * D * 2;    // one K tile == one V tile
   static constexpr int KATOMS = D / 64;          // 128-byte swizzle atoms along D
-  static constexpr int SMEM = 2 * Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 256;  // + barriers
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * KV_STAGES * KV_BYTES + 1024 + 512;  // + barriers
   static constexpr uint32_t TMEM_COLS = 512;     // S0 | S1 | O0 | O1
   static constexpr uint32_t O_COL = 2 * BN;
 };
@@ -77,6 +77,7 @@ struct Params {
   float scale_log2;
   int causal;
   uint32_t* status;
+  uint32_t* work;   // dynamic work queue counter (zeroed before the launch), or nullptr
 };
 
 // ------------------------------------------------------------------ packed fp32 math
@@ -113,6 +114,7 @@ __device__ __forceinline__ float ex2(float x) {
 #define SDPA_HEAD_GROUP 8
 #endif
 constexpr int kHeadGroup = SDPA_HEAD_GROUP;
+constexpr int kItemSlots = 4;   // depth of the in-CTA ring of item ids (dynamic schedule)
 
 // Work item t (0 .. items-1) -> (b * Hq + h, query-tile pair).  Groups of kHeadGroup
 // (batch, head) pairs; inside a group the heaviest query pairs (late, for causal) of all
@@ -156,7 +158,10 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint64_t* p_full = s_full + 2;             // [2 tiles][2 halves of the keys]
   uint64_t* o_done = p_full + 4;             // [2]
   uint64_t* o_free = o_done + 2;             // [2] the epilogue has read O_i
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  uint64_t* item_full = o_free + 2;          // [kItemSlots] an item id was published
+  uint64_t* item_empty = item_full + kItemSlots;   // [kItemSlots] every role has read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kItemSlots);
+  volatile int* s_item = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [kItemSlots]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -187,6 +192,10 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       mbar_init(&o_done[i], 1);
       mbar_init(&o_free[i], 128);
     }
+    for (int i = 0; i < kItemSlots; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 1 + 256);    // the MMA thread and the 256 softmax threads
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -198,6 +207,28 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // The k-th item of this CTA.  Static: blockIdx.x + k * gridDim.x.  Dynamic (p.work set):
+  // the producer takes the next item from the device-wide counter and publishes it in a
+  // small ring; the MMA thread and the softmax threads read it from there, in order.  An id
+  // >= items ends the CTA's loop.
+  auto fetch_item = [&](int k) -> int {     // producer
+    if (p.work == nullptr) return int(blockIdx.x) + k * int(gridDim.x);
+    const int slot = k % kItemSlots;
+    if (!mbar_wait(&item_empty[slot], ((k / kItemSlots) & 1) ^ 1, p.status)) return items;
+    const int t = int(atomicAdd(p.work, 1u));
+    s_item[slot] = t;
+    mbar_arrive(&item_full[slot]);
+    return t;
+  };
+  auto take_item = [&](int k) -> int {      // MMA thread, softmax threads
+    if (p.work == nullptr) return int(blockIdx.x) + k * int(gridDim.x);
+    const int slot = k % kItemSlots;
+    if (!mbar_wait(&item_full[slot], (k / kItemSlots) & 1, p.status)) return items;
+    const int t = s_item[slot];
+    mbar_arrive(&item_empty[slot]);
+    return t;
+  };
+
   if (warp < 4) {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(WG0_REGS));
    if (warp == 0) {
@@ -205,7 +236,9 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (elect_one()) {
       int jg = 0, it = 0;                    // KV tiles loaded so far; items with work
       bool ok = true;
-      for (int t = blockIdx.x; t < items && ok; t += gridDim.x) {
+      for (int k = 0; ok; ++k) {
+        const int t = fetch_item(k);
+        if (t >= items) break;
         int bh, pair;
         item_coords(t, nq, nbh, bh, pair);
         const int q0 = pair * 2 * BM;
@@ -250,7 +283,9 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       int jg = 0, it = 0;
       int pv_g[2] = {0, 0}, acc_items[2] = {0, 0};
       bool ok = true;
-      for (int t = blockIdx.x; t < items && ok; t += gridDim.x) {
+      for (int k = 0; ok; ++k) {
+        const int t = take_item(k);
+        if (t >= items) break;
         int bh, pair;
         item_coords(t, nq, nbh, bh, pair);
         const int q0 = pair * 2 * BM;
@@ -338,7 +373,9 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const float c = p.scale_log2;
     int sg = 0, acc_items = 0;                // S tiles seen, items whose O accumulated
     bool ok = true;
-    for (int t = blockIdx.x; t < items && ok; t += gridDim.x) {
+    for (int k = 0; ok; ++k) {
+      const int t = take_item(k);
+      if (t >= items) break;
       int bh, pair;
       item_coords(t, nq, nbh, bh, pair);
       const int q0 = pair * 2 * BM;
@@ -544,6 +581,19 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   // +15 % non-causal at S = 1024, +10 % / +8 % at 2048, +1-3 % at 4096, even at 8192.
   const int64_t items = int64_t(p.num_ctas_q) * B * Hq;
   const int64_t ctas = std::min<int64_t>(items, enigma::sm_count());
+  // Causal items differ in cost (late query pairs see more keys): from S = 4096 on, CTAs
+  // take items from a device-wide counter in the same order instead of a fixed stride, so
+  // the SMs finish together (a scheduling model of the item costs gives 0.93 -> 0.99 of the
+  // ideal balance at 4096, 0.97 -> 1.00 at 8192; measured +2.5 % at 4096, +0-4 % at 8192,
+  // and -1.5 % at 2048, where the fixed stride stays).  The counter pair is zeroed on the
+  // stream before the launch.
+  p.work = nullptr;
+  if (causal && Sq >= 4096 && items > ctas) {
+    p.work = enigma::work_counters();
+    if (p.work == nullptr) return cudaErrorMemoryAllocation;
+    e = cudaMemsetAsync(p.work, 0, 2 * sizeof(uint32_t), s);
+    if (e != cudaSuccess) return e;
+  }
   const dim3 grid(static_cast<unsigned>(ctas));
   sdpa_fwd_tc_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
