@@ -290,7 +290,9 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0 && nkb > 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(SK_BM, NB * 64, false, true);
+      // M = 64 when the batch fits (AR = 64): half the tensor work of an M = 128 MMA whose
+      // rows 64..127 would be discarded, and half the A bytes read from shared memory.
+      constexpr uint32_t idesc = idesc_bf16_f32(AR == 64 ? 64 : SK_BM, NB * 64, false, true);
       bool ok = true;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % stages;
@@ -311,14 +313,20 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     // Drain row `row` of the accumulator into this CTA's idle ring ([M][PSTRIDE] fp32), then
     // push rows [q R, (q + 1) R) to CTA q of the cluster, into slot [rank] of its receive
     // area, with one bulk copy per CTA.
-    const int q = warp & 3, row = q * 32 + lane;
+    // Accumulator row of this thread's TMEM lane (q * 32 + lane).  M = 128: row = lane.  M = 64:
+    // rows 16 q .. 16 q + 15 sit in the first 16 lanes of lane quarter q; the other 16 lanes
+    // of each quarter hold no row (kNoRow).
+    constexpr int kNoRow = 1 << 20;
+    const int q = warp & 3;
+    const int row = AR == 64 ? (lane < 16 ? q * 16 + lane : kNoRow) : q * 32 + lane;
     if constexpr (EPI == EPI_GATEUP) {   // while the MMAs run
       float t4[4] = {0.f, 0.f, 0.f, 0.f};
       if (row < ea.M) {
 #pragma unroll 4
         for (int t = 0; t < ea.ssq_tiles; ++t) t4[t & 3] += ea.ssq[t * 128 + row];
       }
-      s_rs[row] = 1.0f / sqrtf(((t4[0] + t4[1]) + (t4[2] + t4[3])) / float(ea.ld) + ea.eps);
+      if (row < SK_BM)
+        s_rs[row] = 1.0f / sqrtf(((t4[0] + t4[1]) + (t4[2] + t4[3])) / float(ea.ld) + ea.eps);
     }
     const bool ok = nkb == 0 || mbar_wait(&acc_full, 0, status);
     tc_fence_after();
