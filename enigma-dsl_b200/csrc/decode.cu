@@ -333,18 +333,19 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     float* prow = reinterpret_cast<float*>(ring) + row * S::PSTRIDE;
     const uint32_t taddr = tmem + (uint32_t(q * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < NB * 64; c += 16) {
-      uint32_t v[16];
+    // 32 accumulator columns per TMEM round trip (one load, one wait).
+    for (int c = 0; c < NB * 64; c += 32) {
+      uint32_t v[32];
       if (nkb > 0 && ok) {
-        tmem_ld16(taddr + c, v);
+        tmem_ld32(taddr + c, v);
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int t = 0; t < 16; ++t) v[t] = 0u;
+        for (int t = 0; t < 32; ++t) v[t] = 0u;
       }
       if (row < ea.M) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
+        for (int t = 0; t < 8; ++t)
           reinterpret_cast<float4*>(prow + c)[t] =
               make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
                           __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
