@@ -193,7 +193,7 @@ __device__ __forceinline__ void ck_epilogue(const EpiArgs& e, int tile, int m, i
     const float r = s_rs[m];
     auto sw = [r](float gg, float uu) {
       gg *= r;
-      return gg / (1.0f + __expf(-gg)) * (uu * r);
+      return __fdividef(gg, 1.0f + __expf(-gg)) * (uu * r);   // no IEEE-division subroutine
     };
     st_bf16x4(e.act + int64_t(m) * e.I + j, sw(a0.x, a1.x), sw(a0.y, a1.y), sw(a0.z, a1.z),
               sw(a0.w, a1.w));
