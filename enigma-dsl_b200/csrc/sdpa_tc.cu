@@ -78,6 +78,7 @@ struct Params {
   int causal;
   uint32_t* status;
   uint32_t* work;   // dynamic work queue counter (zeroed before the launch), or nullptr
+  int head_group;   // (batch, head) pairs per group of the item order
 };
 
 // ------------------------------------------------------------------ packed fp32 math
@@ -120,12 +121,12 @@ constexpr int kItemSlots = 4;   // depth of the in-CTA ring of item ids (dynamic
 // (batch, head) pairs; inside a group the heaviest query pairs (late, for causal) of all
 // its heads first.  CTAs running at the same time then share a few heads' K / V in L2, and
 // the last items are light ones.
-__device__ __forceinline__ void item_coords(int t, int nq, int nbh, int& bh, int& pair) {
-  const int grp = t / (kHeadGroup * nq);
-  const int in_grp = t - grp * kHeadGroup * nq;
-  const int gsz = min(kHeadGroup, nbh - grp * kHeadGroup);
+__device__ __forceinline__ void item_coords(int t, int nq, int nbh, int hg, int& bh, int& pair) {
+  const int grp = t / (hg * nq);
+  const int in_grp = t - grp * hg * nq;
+  const int gsz = min(hg, nbh - grp * hg);
   pair = nq - 1 - in_grp / gsz;
-  bh = grp * kHeadGroup + in_grp % gsz;
+  bh = grp * hg + in_grp % gsz;
 }
 
 // KV tiles query tile i (0, 1) of the pair starting at row q0 needs.
@@ -240,7 +241,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int t = fetch_item(k);
         if (t >= items) break;
         int bh, pair;
-        item_coords(t, nq, nbh, bh, pair);
+        item_coords(t, nq, nbh, p.head_group, bh, pair);
         const int q0 = pair * 2 * BM;
         const int n_all = max(kv_tiles(p, q0, 0), kv_tiles(p, q0, 1));
         if (n_all == 0) continue;
@@ -287,7 +288,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int t = take_item(k);
         if (t >= items) break;
         int bh, pair;
-        item_coords(t, nq, nbh, bh, pair);
+        item_coords(t, nq, nbh, p.head_group, bh, pair);
         const int q0 = pair * 2 * BM;
         const int n_kv[2] = {kv_tiles(p, q0, 0), kv_tiles(p, q0, 1)};
         const int n_all = max(n_kv[0], n_kv[1]);
@@ -377,7 +378,7 @@ sdpa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const int t = take_item(k);
       if (t >= items) break;
       int bh, pair;
-      item_coords(t, nq, nbh, bh, pair);
+      item_coords(t, nq, nbh, p.head_group, bh, pair);
       const int q0 = pair * 2 * BM;
       const int n_my = kv_tiles(p, q0, ti);
       if (max(kv_tiles(p, q0, 0), kv_tiles(p, q0, 1)) == 0) continue;
@@ -581,14 +582,17 @@ cudaError_t launch_tc(const void* Q, const void* K, const void* V, void* O, int6
   // +15 % non-causal at S = 1024, +10 % / +8 % at 2048, +1-3 % at 4096, even at 8192.
   const int64_t items = int64_t(p.num_ctas_q) * B * Hq;
   const int64_t ctas = std::min<int64_t>(items, enigma::sm_count());
-  // Causal items differ in cost (late query pairs see more keys): from S = 4096 on, CTAs
-  // take items from a device-wide counter in the same order instead of a fixed stride, so
-  // the SMs finish together (a scheduling model of the item costs gives 0.93 -> 0.99 of the
-  // ideal balance at 4096, 0.97 -> 1.00 at 8192; measured +2.5 % at 4096, +0-4 % at 8192,
-  // and -1.5 % at 2048, where the fixed stride stays).  The counter pair is zeroed on the
-  // stream before the launch.
+  // Causal items differ in cost (late query pairs see more keys): CTAs take items from a
+  // device-wide counter in the item order instead of a fixed stride, so the SMs finish
+  // together; the counter pair is zeroed on the stream before the launch.  Up to S = 2048
+  // the order groups 32 heads (K/V of 32 heads still fit L2 comfortably, and the heavy items
+  // of more heads start first), from 4096 on 8.  Measured (same box): S = 2048 874 -> 911
+  // TFLOP/s, 4096 1023 -> 1048, 8192 +0-4 %, 1024 unchanged; non-causal items are equal and
+  // keep the fixed stride.
   p.work = nullptr;
-  if (causal && Sq >= 4096 && items > ctas) {
+  p.head_group = Sq <= 2048 ? 32 : kHeadGroup;
+  const bool dyn = causal;
+  if (dyn && items > ctas) {
     p.work = enigma::work_counters();
     if (p.work == nullptr) return cudaErrorMemoryAllocation;
     e = cudaMemsetAsync(p.work, 0, 2 * sizeof(uint32_t), s);

@@ -125,8 +125,9 @@ def test_gemm_f32_k4(cuda, m):
     # whose second query tile lies entirely past Sq (Sq = 800), GQA, and Sq < Sk causal
     (2, 64, 8, 800, 800, 128, True), (2, 64, 64, 800, 800, 64, False),
     (1, 160, 160, 300, 1000, 128, True), (4, 48, 16, 1024, 1024, 128, True),
-    # causal from S = 4096 on: items taken from the device-wide work counter
-    (1, 40, 8, 4096, 4096, 128, True), (1, 64, 64, 4352, 4352, 64, True)])
+    # causal: items taken from the device-wide work counter (32-head order up to 2048)
+    (1, 40, 8, 4096, 4096, 128, True), (1, 64, 64, 4352, 4352, 64, True),
+    (3, 40, 8, 2048, 2048, 128, True)])
 def test_sdpa_bf16(cuda, b, hq, hk, sq, sk, d, causal):
     import torch
     from enigma import cuda_ops
