@@ -646,14 +646,90 @@ def while_(cond_fn) -> _While:
     return _While(cond_fn)
 
 
+def _flatten_carry(v, out):
+    """Loop-carried leaves of a value: IRValues and Python numbers (lists / tuples are
+    walked); returns a rebuild spec, or None for a value passed through unchanged (a Tensor,
+    a RegisterTensor, ...)."""
+    if isinstance(v, IRValue):
+        out.append(v)
+        return ("v",)
+    if isinstance(v, (bool, int, float)):
+        out.append(_ensure_ir(v))
+        return ("v",)
+    if isinstance(v, (list, tuple)):
+        specs = [_flatten_carry(e, out) for e in v]
+        if any(sp is None for sp in specs):
+            # a container holding something that cannot be carried: carry nothing from it
+            del out[len(out) - sum(_count(sp) for sp in specs if sp is not None):]
+            return None
+        return ("seq", type(v), specs)
+    return None
+
+
+def _count(spec) -> int:
+    return 1 if spec[0] == "v" else sum(_count(sp) for sp in spec[2])
+
+
+def _rebuild(spec, leaves, pos):
+    if spec[0] == "v":
+        return leaves[pos], pos + 1
+    items = []
+    for sp in spec[2]:
+        it, pos = _rebuild(sp, leaves, pos)
+        items.append(it)
+    return (items if spec[1] is list else spec[1](items)), pos
+
+
+def _enigma_carry_loop(lo, hi, step, body, *values):
+    """A loop rewritten from `for i in enigma.range(...)` (compiler/loops.py): `body(i,
+    *values)` returns the new values; IRValues and numbers (also inside lists / tuples)
+    become loop-carried slots of one traced loop, anything else is passed through.
+    Returns the values after the loop."""
+    leaves: List[IRValue] = []
+    specs = [_flatten_carry(v, leaves) for v in values]
+    if not leaves:
+        with for_range(lo, hi, step) as iv:
+            body(iv, *values)
+        return values
+    with for_range(lo, hi, step, init=leaves) as (iv, carry):
+        cur, pos = [], 0
+        for v, sp in zip(values, specs):
+            if sp is None:
+                cur.append(v)
+            else:
+                r, pos = _rebuild(sp, [carry[i] for i in range(len(leaves))], pos)
+                cur.append(r)
+        res = body(iv, *cur)
+        res = res if isinstance(res, tuple) else (res,)
+        new: List[IRValue] = []
+        for v, sp in zip(res, specs):
+            if sp is not None:
+                got = []
+                sp2 = _flatten_carry(v, got)
+                if sp2 is None or len(got) != _count(sp):
+                    raise EnigmaError("enigma.range(): a loop-carried value changed its structure "
+                                      "inside the loop")
+                new.extend(got)
+        for i, v in enumerate(new):
+            carry[i] = v
+    finals = [carry[i] for i in range(len(leaves))]
+    out, pos = [], 0
+    for v, sp in zip(values, specs):
+        if sp is None:
+            out.append(v)
+        else:
+            r, pos = _rebuild(sp, finals, pos)
+            out.append(r)
+    return tuple(out)
+
+
 class _EnigmaRange:
     """`for i in enigma.range(lo, hi, step)`: a traced loop.
 
-    Inside a kernel trace the body is traced once with a symbolic induction
-    variable; the generator opens the loop region on entry and records the
-    scf_for op when the body finishes.  Values the body rebinds (Python
-    lists, locals) are carried by name only: the trace describes one
-    iteration, which is all the recognizer reads.  Outside a trace it is a
+    Kernel bodies are rewritten before tracing (compiler/loops.py) so that such loops
+    carry the values they rebind (through _enigma_carry_loop).  This generator is what runs
+    when a body could not be rewritten (no source): it traces the body once with a symbolic
+    induction variable and keeps rebound values by name only.  Outside a trace it is a
     plain range.
     """
 

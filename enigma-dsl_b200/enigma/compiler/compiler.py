@@ -53,13 +53,24 @@ def format_ir(builder) -> str:
     def emit(ops, depth):
         for op in ops:
             res = f"{op.result.name}:{op.result.dtype} = " if op.result is not None else ""
+            if op.op == "scf_for" and op.attrs.get("results"):
+                # loop-carried values: results = scf_for(bounds, inits) {iv, iter_args ...
+                # yield}
+                res = ", ".join(f"{r.name}:{r.dtype}" for r in op.attrs["results"]) + " = "
             opnds = ", ".join(getattr(o, "name", repr(o)) for o in op.operands)
             attrs = {k: v for k, v in op.attrs.items() if k not in ("iv", "iter_args",
                                                                      "yield_vals", "results")}
             lines.append("  " * depth + f"{res}{op.op}({opnds}) {attrs if attrs else ''}".rstrip())
             for r in op.regions:
-                lines.append("  " * depth + "{")
+                head = "{"
+                if op.op == "scf_for" and "iv" in op.attrs:
+                    carried = op.attrs.get("iter_args") or []
+                    head = "{ (" + ", ".join([op.attrs["iv"].name] + [a.name for a in carried]) + ")"
+                lines.append("  " * depth + head)
                 emit(r, depth + 1)
+                if op.op == "scf_for" and op.attrs.get("yield_vals"):
+                    lines.append("  " * (depth + 1) + "yield(" + ", ".join(
+                        getattr(v, "name", repr(v)) for v in op.attrs["yield_vals"]) + ")")
                 lines.append("  " * depth + "}")
 
     emit(builder.ops, 1)

@@ -45,6 +45,16 @@ class KernelDef:
         self.fn = fn
         self.name = fn.__name__
         self._sig = inspect.signature(fn)
+        self._traced = None
+
+    @property
+    def traced_fn(self) -> Callable:
+        """The body that is traced: `fn` with its enigma.range loops carrying values
+        (compiler/loops.py), rewritten once."""
+        if self._traced is None:
+            from .loops import rewrite_range_loops
+            self._traced = rewrite_range_loops(self.fn)
+        return self._traced
 
     def __call__(self, *args, **kwargs) -> "KernelHandle":
         return KernelHandle(self, args, kwargs)
@@ -85,7 +95,7 @@ class KernelHandle:
                 b.args.append((a.name, a.buffer_index, a.metal_dtype))
                 seen.add(a.name)
         with b:
-            self.kernel_def.fn(*self.args, **self.kwargs)
+            self.kernel_def.traced_fn(*self.args, **self.kwargs)
         ctx.builder, ctx.grid, ctx.block, ctx.args = b, tuple(grid), tuple(block), self.args
 
 
@@ -116,5 +126,5 @@ def trace_kernel(kdef: KernelDef) -> KernelBuilder:
                 proxies.append(v)
             else:
                 proxies.append(Tensor(p.name, idx, dt))
-        kdef.fn(*proxies)
+        kdef.traced_fn(*proxies)
     return b
