@@ -34,3 +34,20 @@ def test_sharded_ops_match(nccl_group):
     v = torch.randn(2, 2, 256, 128, device="cuda").bfloat16()
     got = shard.sdpa_heads(q, k, v, causal=True, gather=True)
     assert torch.equal(got, cuda_ops.sdpa(q, k, v, causal=True))
+
+
+def test_decode_sequences_one_rank_matches_layer(nccl_group):
+    """decode_sequences with one rank: the rank holds the whole batch, and gathering its
+    output gives the layer's own step (same kernels, same inputs: bit-identical)."""
+    import torch
+    from enigma import shard
+    from enigma.decode_layer import DecodeConfig, DecodeLayer
+    full = DecodeConfig(batch=8, hidden=256, heads_q=4, heads_kv=2, intermediate=512,
+                        cache_len=100, cache_capacity=128)
+    cfg = shard.decode_shard_config(full)
+    assert cfg.batch == 8
+    a = DecodeLayer.random(cfg, seed=3)
+    b = DecodeLayer.random(full, seed=3)
+    x = torch.randn(8, 256, device="cuda").bfloat16()
+    got = shard.decode_sequences(a, x, gather=True)
+    assert torch.equal(got, b.step(x))

@@ -89,3 +89,29 @@ def test_gather_rows_peer_exit_is_reported():
         if p.is_alive():
             p.kill()
     assert out != "no error"
+
+
+def _decode_cfg_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from enigma.decode_layer import DecodeConfig
+    from enigma.shard import decode_shard_config
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        q.put((rank, decode_shard_config(DecodeConfig(batch=7)).batch))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_decode_shard_config_two_ranks():
+    """Sequences of a decode batch split across gloo ranks: 7 -> 4 + 3, nothing else changes."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_decode_cfg_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in ps:
+        p.join(timeout=60)
+    assert got == {0: 4, 1: 3}
