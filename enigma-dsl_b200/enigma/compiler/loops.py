@@ -72,6 +72,24 @@ def _assigned(stmts) -> Set[str]:
     return out
 
 
+def _escapes(stmts, in_loop: bool = False) -> bool:
+    """A return, or a break / continue of this loop (not of a loop nested in it), in the
+    statements; nested function bodies (rewritten inner loops among them) are skipped."""
+    for n in stmts:
+        if isinstance(n, (ast.FunctionDef, ast.AsyncFunctionDef, ast.ClassDef, ast.Lambda)):
+            continue
+        if isinstance(n, ast.Return):
+            return True
+        if isinstance(n, (ast.Break, ast.Continue)) and not in_loop:
+            return True
+        nested_loop = isinstance(n, (ast.For, ast.While, ast.AsyncFor))
+        for field in ("body", "orelse", "handlers", "finalbody"):
+            sub = getattr(n, field, None)
+            if isinstance(sub, list) and _escapes(sub, in_loop or (nested_loop and field == "body")):
+                return True
+    return False
+
+
 class _Rewriter(ast.NodeTransformer):
     def __init__(self, func: ast.FunctionDef):
         self.func = func
@@ -112,10 +130,9 @@ class _Rewriter(ast.NodeTransformer):
             raise SyntaxError("enigma.range(): the loop variable must be a single name")
         if node.orelse:
             raise SyntaxError("enigma.range(): a for ... else loop cannot be traced")
-        for n in ast.walk(ast.Module(body=node.body, type_ignores=[])):
-            if isinstance(n, (ast.Break, ast.Continue, ast.Return)):
-                raise SyntaxError("enigma.range(): break / continue / return inside the loop "
-                                  "cannot be traced")
+        if _escapes(node.body):
+            raise SyntaxError("enigma.range(): break / continue / return inside the loop "
+                              "cannot be traced")
         args = node.iter.args
         if not 1 <= len(args) <= 3:
             raise SyntaxError("enigma.range() takes 1 to 3 arguments")

@@ -87,3 +87,43 @@ def test_break_inside_traced_loop_is_rejected():
 
     with pytest.raises(SyntaxError, match="break"):
         enigma.compile(bad)
+
+
+def test_nested_loops_carry_through_both_levels():
+    """An outer enigma.range loop whose carried sum is updated by an inner loop: the inner
+    loop carries it too, and the outer loop yields the inner loop's result."""
+    @enigma.kernel
+    def nested(A: enigma.f32, Out: enigma.f32):
+        i = enigma.thread_position_in_grid
+        acc = enigma.metal_cast(0.0, "float")
+        for r in enigma.range(4):
+            for c in enigma.range(8):
+                acc = acc + A[i * 32 + enigma.metal_cast(r, "uint") * 8 + enigma.metal_cast(c, "uint")]
+        Out[i] = acc
+
+    from enigma.compiler.kernel import trace_kernel
+    b = trace_kernel(nested)
+    outer = next(op for op in b.ops if op.op == "scf_for")
+    inner = next(op for op in outer.regions[0] if op.op == "scf_for")
+    assert len(outer.attrs["iter_args"]) == 1 and len(inner.attrs["iter_args"]) == 1
+    assert inner.operands[3] is outer.attrs["iter_args"][0]          # inner starts from outer's carry
+    assert outer.attrs["yield_vals"][0] is inner.attrs["results"][0]  # outer yields inner's result
+    store = [op for op in b.ops if op.op == "store"][-1]
+    assert store.operands[1] is outer.attrs["results"][0]
+
+
+def test_closure_values_are_seen_by_the_rewritten_body():
+    scale = 3.0
+
+    @enigma.kernel
+    def scaled(A: enigma.f32, Out: enigma.f32):
+        i = enigma.thread_position_in_grid
+        acc = enigma.metal_cast(0.0, "float")
+        for t in enigma.range(2):
+            acc = acc + A[i] * scale
+        Out[i] = acc
+
+    from enigma.compiler.kernel import trace_kernel
+    b = trace_kernel(scaled)
+    consts = [op.attrs.get("value") for op in b.walk() if op.op == "const"]
+    assert 3.0 in consts
