@@ -290,8 +290,8 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0 && nkb > 0) {
-      // M = 64 when the batch fits (AR = 64): half the tensor work of an M = 128 MMA whose
-      // rows 64..127 would be discarded, and half the A bytes read from shared memory.
+      // M = 64 when the batch fits (AR = 64): no accumulator rows beyond the batch are
+      // computed (the instruction costs the same as M = 128 on the tensor pipe).
       constexpr uint32_t idesc = idesc_bf16_f32(AR == 64 ? 64 : SK_BM, NB * 64, false, true);
       bool ok = true;
       for (int i = 0; i < nkb; ++i) {
