@@ -73,7 +73,7 @@ struct EpiArgs {
 };
 
 constexpr int CK_THREADS = 192;
-constexpr int CK_MAX_CLUSTER = 8;    // portable cluster size
+constexpr int CK_MAX_CLUSTER = 16;   // non-portable cluster size (opted in at launch)
 
 // Shared memory: `stages` A slots of AR rows (AR = 64 when M <= 64, else 128), `stages` B
 // slots, then the receive area.  The MMA always reads 128 A rows; with AR = 64 rows 64..127
@@ -567,6 +567,8 @@ cudaError_t cluster_gemm_ar(const void* A, const void* Bw, int64_t M, int64_t n_
   const int smem = 1024 + stages * S::STAGE + recv;
   auto kern = gemm_cluster_kernel<EPI, NB, AR>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess && cs > 8)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(tiles), unsigned(cs));
