@@ -384,6 +384,8 @@ def _decode_side(hbm_peak, world=1, rank=0):
     _, ms_warm = _timed_max(fn, 50, world, stream)
     kv = 2 * cfg.batch * cfg.heads_kv * (cfg.cache_len + 1) * cfg.head_dim * 2
     byts = layer.weight_bytes() + kv   # this rank's bytes per step
+    del layer
+    stack = _decode_stack(cfg, world, stream)
     return {"ms": round(ms, 4), "tokens_per_s": round(full.batch / (ms * 1e-3), 1),
             "n_gpus": world, "batch_per_gpu": cfg.batch,
             "algorithmic_bytes_per_gpu": byts, "gbs_per_gpu": round(byts / (ms * 1e-3) / 1e9, 1),
@@ -391,7 +393,43 @@ def _decode_side(hbm_peak, world=1, rank=0):
             "l2": "flushed (256 MB read) before every step",
             "ms_back_to_back": round(ms_warm, 4),
             "note": "weights (replicated) + this rank's KV read once per step; back to back, "
-                    "L2 (126 MB) can hold part of the 97 MB working set"}
+                    "L2 (126 MB) can hold part of the 97 MB working set",
+            "stack": stack | {"gbs_per_gpu": round(byts / (stack["ms_per_layer"] * 1e-3) / 1e9, 1),
+                              "frac_hbm": round(byts / (stack["ms_per_layer"] * 1e-3) / 1e9
+                                                / hbm_peak, 4)}}
+
+
+def _decode_stack(cfg, world, stream, n_layers=8):
+    """The same step as one layer of a model: n_layers distinct layers (own weights and KV
+    caches, ~0.78 GB together, six times the 126 MB L2, so no flush is needed) chained
+    out -> x in one CUDA graph, the way a serving step runs a layer stack; time per layer =
+    graph time / n_layers.  The single-layer figure above pays the graph launch and the
+    event pair once per layer; here they are paid once per stack."""
+    import torch
+    from enigma.decode_layer import DecodeLayer
+    layers = [DecodeLayer.random(cfg, seed=100 + i) for i in range(n_layers)]
+    xs = [torch.randn(cfg.batch, cfg.hidden, device="cuda").bfloat16()]
+    xs += [torch.empty_like(xs[0]) for _ in range(n_layers)]
+
+    def chain():
+        for i, lyr in enumerate(layers):
+            lyr.step(xs[i], out=xs[i + 1])
+
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        chain()                      # first launches (per-device setup) outside capture
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        chain()
+    for _ in range(5):
+        graph.replay()
+    _, ms = _timed_max(graph.replay, 30, world, stream)
+    del graph, layers, xs
+    return {"layers": n_layers, "ms_per_layer": round(ms / n_layers, 4),
+            "l2": f"{n_layers} distinct layers per graph (~{n_layers * 97} MB), larger than L2; "
+                  "no flush"}
 
 
 def _sdpa_tc_available() -> bool:

@@ -36,6 +36,11 @@ cudaError_t rmsnorm_launch(int dtype, const void* x, const void* w, void* y, int
 // Same, with the SM count given (no per-device state is touched).
 cudaError_t rmsnorm_launch_sms(int dtype, const void* x, const void* w, void* y, int64_t rows,
                                int64_t hidden, float eps, int sms, cudaStream_t s);
+// The decode step's input norm (bf16): launched as a programmatic dependent when the row
+// is at most 128 16-byte vectors (hidden <= 1024), so in a layer stack it is resident
+// before the previous layer's last kernel ends; else the same as rmsnorm_launch_sms.
+cudaError_t rmsnorm_launch_pdl_bf16(const void* x, const void* w, void* y, int64_t rows,
+                                    int64_t hidden, float eps, int sms, cudaStream_t s);
 cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
                              int64_t K, cudaStream_t s);
 cudaError_t gemm_f32_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,

@@ -615,7 +615,7 @@ cudaError_t decode_layer_run(const enigma_decode_layer_desc& d, const void* x, v
   EpiArgs ea = {};
   ea.M = B;
   // 1. input RMSNorm
-  ENIGMA_TRY(rmsnorm_launch_sms(ENIGMA_DTYPE_BF16, x, d.w_in_norm, bfp(l.xn), B, H, d.eps, sms, s));
+  ENIGMA_TRY(rmsnorm_launch_pdl_bf16(x, d.w_in_norm, bfp(l.xn), B, H, d.eps, sms, s));
   // 2. QKV projection + RoPE + KV-cache append at `position` (+ attention counters zeroed)
   ea.Hq = Hq;
   ea.Hkv = Hkv;

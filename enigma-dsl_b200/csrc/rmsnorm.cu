@@ -70,7 +70,10 @@ __device__ __forceinline__ uint4 pack<__nv_bfloat16>(const float* f) {
 // THREADS threads per row, NV 16-byte vectors per thread.  Without PRED the row is
 // exactly THREADS*NV vectors; with PRED it has row_vecs <= THREADS*NV vectors and the
 // vectors past the end are skipped (e.g. hidden 896 bf16 = 112 vectors on 128 threads).
-template <typename T, int THREADS, int NV, bool PRED = false>
+// PDL: launched as a programmatic dependent (the decode step's first kernel, which in a
+// layer stack follows the previous layer's last GEMM): the next kernel may start its
+// prologue at once, and every read of x waits until the previous kernel has completed.
+template <typename T, int THREADS, int NV, bool PRED = false, bool PDL = false>
 __global__ void __launch_bounds__(THREADS)
 rmsnorm_row_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
                    int64_t rows, float inv_hidden, float eps, int row_vecs) {
@@ -78,6 +81,10 @@ rmsnorm_row_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restri
   constexpr int kWarps = THREADS / 32;
   const int64_t kRowVecs = PRED ? row_vecs : int64_t(THREADS) * NV;
   __shared__ float red[kWarps];
+  if constexpr (PDL) {
+    enigma_sm100::griddep_launch_dependents();
+    enigma_sm100::griddep_wait();
+  }
 
   const int tid = threadIdx.x;
   const uint4* wv = reinterpret_cast<const uint4*>(w);
@@ -160,13 +167,28 @@ rmsnorm_generic_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __re
   }
 }
 
-template <typename T, int THREADS, int NV, bool PRED = false>
+template <typename T, int THREADS, int NV, bool PRED = false, bool PDL = false>
 cudaError_t launch_row(const void* x, const void* w, void* y, int64_t rows, int64_t hidden,
                        float eps, int sms, cudaStream_t s) {
   // Enough CTAs to fill every SM several times over; each CTA strides over rows.
   const int64_t max_ctas = int64_t(sms) * (2048 / THREADS) * 8;
   const int grid = int(rows < max_ctas ? rows : max_ctas);
   enigma::note_kernel("rmsnorm_row_kernel");
+  if constexpr (PDL) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(THREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rmsnorm_row_kernel<T, THREADS, NV, PRED, true>,
+                              static_cast<const T*>(x), static_cast<const T*>(w),
+                              static_cast<T*>(y), rows, 1.0f / float(hidden), eps,
+                              int(hidden / Vec<T>::kElems));
+  }
   rmsnorm_row_kernel<T, THREADS, NV, PRED><<<grid, THREADS, 0, s>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), static_cast<T*>(y), rows,
       1.0f / float(hidden), eps, int(hidden / Vec<T>::kElems));
@@ -217,6 +239,19 @@ cudaError_t rmsnorm_launch_sms(int dtype, const void* x, const void* w, void* y,
   if (rows == 0) return cudaSuccess;
   if (dtype == ENIGMA_DTYPE_F32) return dispatch<float>(x, w, y, rows, hidden, eps, sms, s);
   return dispatch<__nv_bfloat16>(x, w, y, rows, hidden, eps, sms, s);
+}
+
+cudaError_t rmsnorm_launch_pdl_bf16(const void* x, const void* w, void* y, int64_t rows,
+                                    int64_t hidden, float eps, int sms, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  using T = __nv_bfloat16;
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(y) % 16 == 0) && (hidden % 8 == 0);
+  const int64_t vecs = hidden / 8;
+  if (aligned && vecs == 128) return launch_row<T, 128, 1, false, true>(x, w, y, rows, hidden, eps, sms, s);
+  if (aligned && vecs < 128) return launch_row<T, 128, 1, true, true>(x, w, y, rows, hidden, eps, sms, s);
+  return dispatch<T>(x, w, y, rows, hidden, eps, sms, s);
 }
 
 cudaError_t rmsnorm_launch(int dtype, const void* x, const void* w, void* y, int64_t rows,
