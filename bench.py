@@ -450,6 +450,23 @@ def _decode_stack(cfg, world, stream, n_layers=8):
                   "no flush"}
 
 
+def _cudnn_sdpa_ms(q, k, v, causal, warm, steps, stream):
+    """Device ms of torch's scaled_dot_product_attention restricted to the cuDNN fused
+    attention backend on the same tensors (a library reference point, as cuBLAS is for the
+    GEMM), or None when that backend refuses the case."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    try:
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            fn = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal)  # noqa: E731
+            for _ in range(warm):
+                fn()
+            return _time_device(fn, steps, stream)
+    except RuntimeError:
+        return None
+
+
 def _sdpa_tc_available() -> bool:
     from enigma import _native
     return hasattr(_native.lib(), "enigma_sdpa_bf16")
@@ -524,11 +541,17 @@ def run_sweep(args):
             for _ in range(warm):
                 fn()
             ms = _time_device(fn, steps, stream)
-            tf = (2 if causal else 4) * B * H * S * S * D / (ms * 1e-3) / 1e12
+            fl = (2 if causal else 4) * B * H * S * S * D
+            tf = fl / (ms * 1e-3) / 1e12
+            ref = _cudnn_sdpa_ms(q, k, v, causal, warm, steps, stream)
             print(json.dumps({"config": 4, "op": "sdpa_bf16", "S": S, "causal": causal,
                               "ms": round(ms, 4), "value": round(tf, 1), "unit": "TFLOP/s",
                               "frac_tensor": round(tf / tc_peak, 4), "timing": "back to back",
-                              "flops": "causal 2BHS^2D, non-causal 4BHS^2D"}), flush=True)
+                              "flops": "causal 2BHS^2D, non-causal 4BHS^2D",
+                              "cudnn_same_loop_tflops": None if ref is None else
+                              round(fl / (ref * 1e-3) / 1e12, 1),
+                              "vs_cudnn_same_loop": None if ref is None else
+                              round(ref / ms, 4)}), flush=True)
         del q, k, v, o
     print(json.dumps({"config": 5, "op": "decode_layer"} | _decode_side(hbm_peak)), flush=True)
 
