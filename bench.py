@@ -723,13 +723,20 @@ def run_single_op(args):
         o = torch.empty_like(q)
         causal = args.only == "sdpa_causal"
         fn = lambda: cuda_ops.sdpa(q, k, v, causal=causal, out=o)  # noqa: E731
+        if args.cudnn:   # the library reference point instead: cuDNN fused attention
+            import torch.nn.functional as F
+            from torch.nn.attention import SDPBackend, sdpa_kernel
+            ctx = sdpa_kernel(SDPBackend.CUDNN_ATTENTION)
+            ctx.__enter__()
+            fn = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal)  # noqa: E731
         work, unit = (2 if causal else 4) * B * H * n * n * D, "TFLOP/s"
     for _ in range(args.warmup):
         fn()
     ms = _time_device(fn, args.steps, stream)
     cuda_ops.synchronize(0)
     print(json.dumps({"op": args.only, "size": n, "ms": round(ms, 4),
-                      "value": round(work / (ms * 1e-3) / 1e12, 1), "unit": unit}), flush=True)
+                      "value": round(work / (ms * 1e-3) / 1e12, 1), "unit": unit,
+                      "impl": "cudnn" if args.cudnn else "enigma"}), flush=True)
 
 
 def main():
@@ -747,6 +754,8 @@ def main():
                     default=None,
                     help="time one operator alone (profiling case)")
     ap.add_argument("--graph", action="store_true", help="--only decode: replay a CUDA graph")
+    ap.add_argument("--cudnn", action="store_true",
+                    help="--only sdpa|sdpa_causal: time cuDNN's fused attention (torch SDPA) instead")
     ap.add_argument("--size", type=int, default=4096, help="--only: n for GEMM n^3, S for SDPA")
     ap.add_argument("--hidden", type=int, default=HIDDEN, help="--only rmsnorm: row width")
     ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16", help="--only rmsnorm")
