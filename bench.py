@@ -353,6 +353,14 @@ def _ops_side(world, rank, hbm_peak, tc_peak, peak_kind):
         "rows_per_gpu": hi - lo, "frac": round(tf / world / tc_peak, 4), "peak": tc_peak,
         "peak_kind": peak_kind + " burst, per GPU", "clocks": clk.summary(),
         "allgather_C": _allgather_ms(c, world)}
+    # cuBLAS (torch.matmul) on the same shard, timed the same way: the library reference point.
+    ref = lambda: torch.matmul(a, b, out=c)  # noqa: E731
+    _settle()
+    for _ in range(3):
+        ref()
+    _, ms_ref = _timed_max(ref, 20, world, stream)
+    res["gemm_bf16_8192"]["cublas_same_loop_tflops"] = round(2 * n ** 3 / (ms_ref * 1e-3) / 1e12, 1)
+    res["gemm_bf16_8192"]["vs_cublas_same_loop"] = round(ms_ref / ms_max, 4)
     del a, b, c
     B, H, S, D = 8, 32, 8192, 128
     blo, bhi = shard.shard_range(B, world, rank)
@@ -374,6 +382,15 @@ def _ops_side(world, rank, hbm_peak, tc_peak, peak_kind):
             "flops_convention": "causal 2*B*H*S^2*D, non-causal 4*B*H*S^2*D",
             "clocks": clk.summary(),
             "allgather_O": _allgather_ms(o, world) if not causal else None}
+        # cuDNN fused attention on the same shard (torch SDPA, cuDNN backend), timed the same way.
+        _settle()
+        ref_ms = _cudnn_sdpa_ms(q, k, v, causal, 3, 10, stream)
+        # every rank joins the max (1e30 stands for "backend refused"), so none waits alone
+        ref_ms = _max_over_ranks(1e30 if ref_ms is None else ref_ms, world)
+        if ref_ms < 1e29:
+            key = f"sdpa_bf16_{'causal' if causal else 'noncausal'}_8x32x8192x128"
+            res[key]["cudnn_same_loop_tflops"] = round(fl / (ref_ms * 1e-3) / 1e12, 1)
+            res[key]["vs_cudnn_same_loop"] = round(ref_ms / ms_max, 4)
     del q, k, v, o
     _settle()
     res["decode_layer_config5"] = _decode_side(hbm_peak, world, rank)
