@@ -225,15 +225,21 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 //                       the leader's full[stage] barrier (cta_group::2 form of the load)
 //   leader, warp 1      MMA issue; releases a stage / publishes an accumulator by
 //                       committing to the barrier in both CTAs
-//   both CTAs, warps 2-5 epilogue of the CTA's 128 rows; arrive on the leader's
-//                       acc_empty (256 arrivals per accumulator)
+//   both CTAs, warps 2-5 epilogue of the CTA's 128 rows (32 per warp, through a
+//                       swizzled shared-memory box and a TMA tile store per 64 columns);
+//                       arrive on the leader's acc_empty (256 arrivals per accumulator)
 constexpr int P_BM = 256;                              // tile rows per pair
 constexpr int P_BN = 256;                              // tile columns per pair
 constexpr int P_STAGES = 6;
 constexpr int P_A_BYTES = (P_BM / 2) * BK * 2;         // 16 KB: this CTA's 128 rows
 constexpr int P_B_BYTES = BK * (P_BN / 2) * 2;         // 16 KB: this CTA's 128 columns
 constexpr int P_STAGE = P_A_BYTES + P_B_BYTES;
-constexpr int P_SMEM = P_STAGES * P_STAGE + 1024 + 256;
+// Epilogue staging: per epilogue warp two 32-row x 64-column bf16 boxes (4 KB each, 128-byte
+// swizzle) that TMA stores to C while the warp fills the other one.
+constexpr int P_C_BOX_BYTES = 32 * 64 * 2;
+constexpr int P_C_BYTES = (EPI_THREADS / 32) * 2 * P_C_BOX_BYTES;
+constexpr int P_SMEM = P_STAGES * P_STAGE + P_C_BYTES + 1024 + 256;
+static_assert(P_SMEM <= 232448, "pair GEMM shared memory");
 
 // HALF: every 256 x 256 tile runs as two 256 x 128 halves (MMA N = 128, one 64-column B box
 // per CTA), for problems with fewer tiles than CTA pairs: twice the pairs get work (1024^3:
@@ -241,14 +247,16 @@ constexpr int P_SMEM = P_STAGES * P_STAGE + 1024 + 256;
 template <bool HALF>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, __nv_bfloat16* __restrict__ C,
-                      int M, int N, int K, uint32_t* status) {
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
+                      uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + P_STAGES * P_A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE);
+  uint8_t* sC = smem + P_STAGES * P_STAGE;                 // epilogue staging (1024-aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sC + P_C_BYTES);
   uint64_t* empty = full + P_STAGES;
   uint64_t* acc_full = empty + P_STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -262,6 +270,7 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
     for (int s = 0; s < P_STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -351,50 +360,60 @@ gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (both CTAs): this CTA's 128 rows of each 256-row tile
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of each 256-row tile, 32 per
+    // warp.  Per 64-column chunk: tcgen05.ld -> bf16 -> a 128-byte-swizzled 32 x 64 box in
+    // this warp's staging buffer -> one TMA tile store (clipped at ragged edges), while the
+    // warp fills its other buffer.  The accumulator is released once its last chunk is in
+    // registers, before the stores complete.
     const int quarter = warp & 3;
-    const int row_in_tile = int(rank) * 128 + quarter * 32 + lane;
+    const int row_in_tile = int(rank) * 128 + quarter * 32;    // first row of this warp
+    uint8_t* stg = sC + (warp - 2) * 2 * P_C_BOX_BYTES;
+    const uint32_t sw = uint32_t(lane & 7);
     const uint32_t acce0_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
-    int acc = 0;
+    int acc = 0, buf = 0;
     uint32_t acc_phase = 0;
     for (int t = pair_id; t < num_tiles; t += num_pairs) {
       int mb, nb;
       sched.coords(HALF ? t >> 1 : t, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, status)) break;
       tc_fence_after();
-      const int row = mb * P_BM + row_in_tile;
+      const int row0 = mb * P_BM + row_in_tile;
       const int col0 = nb * P_BN + (HALF ? (t & 1) * UW : 0);
-      __nv_bfloat16* crow = C + int64_t(row) * N;
       const uint32_t taddr = tmem_base + acc * P_BN + (uint32_t(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < UW; c += 32) {
-        uint32_t r0[16], r1[16];
-        tmem_ld16(taddr + c, r0);
-        tmem_ld16(taddr + c + 16, r1);
+      for (int c = 0; c < UW; c += 64) {
+        uint32_t r[64];
+        tmem_ld32(taddr + c, r);
+        tmem_ld32(taddr + c + 32, r + 32);
         tmem_wait_ld();
-        if (row < M && col0 + c < N) {
-          uint32_t p[16];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            p[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
-            p[8 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
-          }
-          __nv_bfloat16* dst = crow + col0 + c;
-          if (col0 + c + 32 <= N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
-          } else {
-            const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(p);
-            for (int i = 0; i < 32 && col0 + c + i < N; ++i) dst[i] = pb[i];
-          }
+        if (c + 64 >= UW) {           // every TMEM read of this accumulator is done
+          tc_fence_before();
+          mbar_arrive_cluster(acce0_leader + acc * 8);
         }
+        if (lane == 0) bulk_wait_group_read<1>();   // the store two chunks back has read buf
+        __syncwarp();
+        uint8_t* box = stg + buf * P_C_BOX_BYTES + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+          v.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+          v.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+          v.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+          *reinterpret_cast<uint4*>(box + ((uint32_t(j) ^ sw) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (row0 < M && col0 + c < N) tma_store_2d(&tmC, stg + buf * P_C_BOX_BYTES, col0 + c, row0);
+          bulk_commit_group();        // (an empty group when the box lies past M or N)
+        }
+        buf ^= 1;
       }
-      tc_fence_before();
-      mbar_arrive_cluster(acce0_leader + acc * 8);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -483,7 +502,9 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
     cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    if (M >= 256 && N >= 256) {
+    CUtensorMap tc;
+    if (M >= 256 && N >= 256 && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
+        make_tmap_bf16_2d(&tc, C, M, N, N, 64, 32)) {
       // CTA-pair kernel: B boxes of the pair's two N halves, A boxes of 128 rows.
       const int64_t ptiles = ((M + P_BM - 1) / P_BM) * ((N + P_BN - 1) / P_BN);
       const bool half = 2 * ptiles <= sm_count() / 2;
@@ -492,8 +513,7 @@ cudaError_t gemm_bf16_launch(const void* A, const void* B, void* C, int64_t M, i
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
       if (e != cudaSuccess) return e;
       const int pairs = int(std::min<int64_t>(half ? 2 * ptiles : ptiles, sm_count() / 2));
-      kern<<<2 * pairs, THREADS, P_SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), int(M),
-                                              int(N), int(K), status);
+      kern<<<2 * pairs, THREADS, P_SMEM, s>>>(ta, tb, tc, int(M), int(N), int(K), status);
       return cudaGetLastError();
     }
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
